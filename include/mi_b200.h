@@ -1,0 +1,158 @@
+/*
+ * mi_b200.h -- C ABI of the B200 (sm_100a) Mamba-Integer hot path.
+ *
+ * Conventions (all entry points):
+ *   - every buffer is caller-owned device memory (the library never allocates
+ *     or frees, except where an entry point says so);
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     work is enqueued on it with no host synchronisation;
+ *   - the return value is a status code: MI_OK (0) or a negative MI_ERR_*;
+ *     argument/shape errors are detected on the host before any launch;
+ *   - device-side conditions (integer overflow, a bounded wait that expired)
+ *     are recorded in a per-device error word read by mi_device_error().
+ *
+ * Each declaration names the reference interface it replaces
+ * (paths relative to the reference repository).
+ */
+#ifndef MI_B200_H
+#define MI_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MI_OK 0
+#define MI_ERR_INVALID (-1)     /* bad pointer, size or stride */
+#define MI_ERR_UNSUPPORTED (-2) /* shape/config this build does not handle */
+#define MI_ERR_CUDA (-3)        /* CUDA runtime / driver error at launch */
+#define MI_ERR_DEVICE (-4)      /* device error word was set (see mi_device_error) */
+
+/* device error word bits */
+#define MI_DEV_OVERFLOW 0x1     /* integer scan: a state or output left int32 */
+#define MI_DEV_TIMEOUT 0x2      /* a bounded mbarrier wait expired */
+#define MI_DEV_PRECOND 0x4      /* an input outside the kernel's stated range */
+
+int mi_version(void);
+const char* mi_status_string(int status);
+
+/* Reads (and clears, if `clear`) the device error word of the current device.
+ * Synchronises `stream`. */
+int mi_device_error(int* out, int clear, void* stream);
+
+/*
+ * Integer dyadic selective scan.
+ *   h[b,d,j] <- ((int64)h * n[d,j]) >> k  +  B[b,t,j] * x[b,t,d]
+ *   y[b,t,d]  = sum_j C[b,t,j] * h[b,d,j]
+ * x [batch,L,D], B/C [batch,L,N], n [D,N], h_io [batch,D,N] (initial state
+ * in, final state out), y [batch,L,D] int32 (y32) or int64 (y64): exactly one
+ * of y32 / y64 is non-NULL.  Preconditions checked on the device (error word
+ * MI_DEV_PRECOND): 0 <= n <= 2^k; |x|, |B|, |C| <= 32767.  A state that
+ * leaves int32, or a y32 value that does, sets MI_DEV_OVERFLOW.
+ * Supports N = 16; 1 <= k <= 30.
+ * Replaces: launch_dyadic_scan, src/cuda_kernels/dyadic_mamba_kernel.cu:135-153
+ * (state update :53-59), extended with the B/C terms of the selective scan.
+ */
+int mi_scan_i32(const int32_t* x, const int32_t* B, const int32_t* C, const int32_t* n, int k,
+                int32_t* y32, int64_t* y64, int32_t* h_io, int batch, int L, int D, int N,
+                void* stream);
+
+/*
+ * BitShiftNorm forward (CPU-path semantics): centre (twice: BitShiftNorm.forward
+ * then BitShiftNormFunction.forward; once if center_once), var = mean(xc^2),
+ * power-of-2 scale s from the threshold table, y = ((xc*s)*gamma)*step.
+ * x, y [T,D]; gamma [D]; step [1] (device); inv_rms [T] (may be NULL).
+ * D % 32 == 0, 32 <= D <= 1024.
+ * Replaces: fast_bitshift_norm, src/triton_kernels/bitnet_kernels.py:295
+ * (and launch_bitshift_norm, src/cuda_kernels/bitshift_norm.cu:97-114).
+ */
+int mi_bitshift_norm(const float* x, const float* gamma, const float* step, float* y, float* inv_rms,
+                     int T, int D, int center_once, void* stream);
+
+/*
+ * Per-token absmax int8 quantisation (activation_quant_dynamic):
+ *   s = max(amax|x|, 1e-8); xq = clamp(rne(x * (127 * (1/s))), +-127);
+ *   xscale = s / 127.
+ * x [T, >=K] row stride ldx; xq [T, >=K] row stride ldq (int8).
+ * Replaces: fast_quantize_activations, src/triton_kernels/bitnet_kernels.py:98.
+ */
+int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
+                     void* stream);
+
+/*
+ * Row pre-pass in front of a BitLinear: optional residual update, BitShiftNorm,
+ * int8 quantisation, in one pass over each row.
+ *   source row r = ids ? emb[ids[t]] : x[t] (+ delta[t] * (*res_gate) if delta)
+ *   (an id outside [0, vocab) reads a zero row and sets MI_DEV_PRECOND)
+ *   x_out[t] = r (if x_out; the new residual stream)
+ *   y = BitShiftNorm(r); (y_norm[t] = y if y_norm)
+ *   (xq[t], xscale[t]) = quantise(y)
+ * D % 32 == 0, 32 <= D <= 1024.
+ * Replaces the sequence BitShiftNorm -> activation_quant_dynamic in
+ * src/mamba_integer_model.py:397-400 / :447 -> :398 / :492-494.
+ */
+int mi_rowprep(const float* x, const float* delta, const float* res_gate, const int64_t* ids,
+               const float* emb, int vocab, float* x_out, const float* gamma, const float* step, float* y_norm,
+               int8_t* xq, float* xscale, int T, int D, void* stream);
+
+/* BitLinear epilogues */
+#define MI_EPI_I32 0        /* out int32 [M,N]: the raw accumulators */
+#define MI_EPI_F32_SCALED 1 /* out fp32: acc * (w_scale * a_scale[m]) [* out_scale] */
+
+/*
+ * Ternary BitLinear contraction on tcgen05 (kind::i8, int32 accumulators in
+ * TMEM).  A int8 [M,K] (row stride lda), W int8 ternary [N,K] (dense rows),
+ * out [M,N] row stride ldo.  a_scale [M], w_scale [1], out_scale [1] are
+ * device pointers (out_scale may be NULL).  K % 16 == 0, lda % 16 == 0,
+ * N % 16 == 0.
+ * Replaces: launch_bitlinear, src/cuda_kernels/bitlinear.cu:74-90, and the
+ * matmul + rescale of BitLinear.forward, src/rational_bitnet.py:204-208.
+ */
+int mi_bitlinear_i8(const int8_t* A, int lda, const int8_t* W, const float* a_scale,
+                    const float* w_scale, const float* out_scale, void* out, int ldo, int M, int N,
+                    int K, int epilogue, void* stream);
+
+/*
+ * Causal depthwise conv (4 taps, bias first then one FMA per tap) +
+ * ste_clamp(-50, 50) + squareplus (3 Newton steps), then int8 quantisation of
+ * each row of the activation.
+ * xz rows [batch*L] with stride ldx: the first D columns are the conv input;
+ * w [D,4], bias [D]; act [batch*L, D]; xq [batch*L, D]; xscale [batch*L].
+ * Replaces: conv1d + fused_squareplus_clamp, src/mamba_integer_model.py:404-411
+ * (fused_squareplus_clamp: src/triton_kernels/fused_activations.py:229).
+ */
+int mi_conv_act_quant(const float* xz, int ldx, const float* w, const float* bias, float* act,
+                      int8_t* xq, float* xscale, int batch, int L, int D, void* stream);
+
+/*
+ * Selective-scan section of MambaIntegerBlock from the dt_proj output on:
+ * decay clamp, dt, u = (x*dt)*B, convex dyadic scan h = h*d + (1-d)*u with
+ * d = n/2^15, y = sum_n h*C (FMA, n ascending), gate y*sigmoid_alg(z).
+ * act [batch*L, D]; bc rows (stride ldbc): B at [0,N), C at [N,2N);
+ * modraw [batch*L, D]; z rows stride ldz; base [D,N]; y [batch*L, D].
+ * amax (optional, [batch*L], zero-filled by the caller) receives max|y| per row.
+ * N == 16.
+ * Replaces: DyadicScanFunction.apply / dyadic_scan_triton_fast
+ * (src/mamba_integer_model.py:419-444, src/triton_kernels/dyadic_scan.py:462).
+ */
+int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw, const float* z,
+                int ldz, const float* base, float* y, float* amax, int batch, int L, int D, int N,
+                void* stream);
+
+/* Convex dyadic scan on materialised inputs: h = h*(n/2^15) + (1-n/2^15)*u.
+ * u, nums, h [batch, L, DN].
+ * Replaces: dyadic_scan_triton_fast(u, nums), src/triton_kernels/dyadic_scan.py:462. */
+int mi_scan_convex(const float* u, const float* nums, float* h, int batch, int L, int DN, void* stream);
+
+/* Element-wise ops (n elements, contiguous).
+ * Replace fused_squareplus_clamp / fused_ste_clamp / fused_sigmoid_gate,
+ * src/triton_kernels/fused_activations.py:229, :511, :399. */
+int mi_squareplus_clamp(const float* x, float* y, int64_t n, float lo, float hi, void* stream);
+int mi_ste_clamp(const float* x, float* y, int64_t n, float lo, float hi, void* stream);
+int mi_sigmoid_gate(const float* y, const float* z, float* out, int64_t n, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MI_B200_H */

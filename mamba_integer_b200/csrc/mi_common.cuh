@@ -1,0 +1,115 @@
+// mi_common.cuh -- shared device helpers for the sm_100a Mamba-Integer kernels.
+// Included once by the unity translation unit mi_b200_unity.cu.
+//
+// Floating-point stages reproduce the reference CPU path operation by
+// operation.  Every product and sum below is written with an explicit
+// round-to-nearest intrinsic so that no build flag can contract a*b+c into a
+// fused multiply-add; the only FMAs are the ones written as __fmaf_rn, at the
+// places where the reference itself accumulates with FMA (conv taps, h.C).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/mi_b200.h"
+
+namespace mi {
+
+// per-device error word (bits MI_DEV_*), read by mi_device_error().  The
+// library is built as one translation unit (mi_b200_unity.cu), so this is
+// the single definition.
+__device__ int g_dev_error;
+
+__device__ __forceinline__ void raise_dev_error(int bits) { atomicOr(&g_dev_error, bits); }
+
+// torch.clamp(x, lo, hi) on fp32: NaN propagates.
+__device__ __forceinline__ float clamp_t(float x, float lo, float hi) {
+    if (x != x) return x;
+    if (x < lo) return lo;
+    if (x > hi) return hi;
+    return x;
+}
+
+// ste_clamp forward value x + (clamp(x) - x)  (src/mamba_integer_model.py:136-141)
+__device__ __forceinline__ float ste_clamp(float x, float lo, float hi) {
+    float c = clamp_t(x, lo, hi);
+    return __fadd_rn(x, __fsub_rn(c, x));
+}
+
+// _rsqrt_newton (src/mamba_integer_model.py:80-102): guess table, 3 Newton
+// steps r = r * (1.5 - ((0.5*y)*r)*r), each clamped to [1e-6, 1e3].
+__device__ __forceinline__ float rsqrt_newton(float y) {
+    y = clamp_t(y, 1e-6f, 1e6f);
+    float r = (y > 16.0f) ? 0.125f : 0.5f;
+    if (y > 64.0f) r = 0.0625f;
+    if (y > 256.0f) r = 0.03125f;
+    if (y < 4.0f) r = 1.0f;
+    if (y < 1.0f) r = 2.0f;
+    if (y < 0.25f) r = 4.0f;
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        float t = __fmul_rn(0.5f, y);
+        t = __fmul_rn(t, r);
+        t = __fmul_rn(t, r);
+        t = __fsub_rn(1.5f, t);
+        r = __fmul_rn(r, t);
+        r = clamp_t(r, 1e-6f, 1e3f);
+    }
+    return r;
+}
+
+// _squareplus_rational (src/mamba_integer_model.py:105-121)
+__device__ __forceinline__ float squareplus(float x) {
+    float ysq = __fadd_rn(__fmul_rn(x, x), 4.0f);
+    float ys = clamp_t(ysq, 1e-6f, 1e6f);
+    float r = rsqrt_newton(ys);
+    float s = clamp_t(__fmul_rn(ys, r), 0.0f, 1e3f);
+    return __fmul_rn(0.5f, __fadd_rn(x, s));
+}
+
+// y * _sigmoid_algebraic(z) = y * (0.5 + (0.5*z) / (1 + |z|))  (:124-132, :444)
+__device__ __forceinline__ float sigmoid_gate(float y, float z) {
+    float num = __fmul_rn(0.5f, z);
+    float den = __fadd_rn(1.0f, fabsf(z));
+    float s = __fadd_rn(0.5f, __fdiv_rn(num, den));
+    return __fmul_rn(y, s);
+}
+
+// _find_power_of_2_scale (src/mamba_integer_model.py:144-184)
+__device__ __forceinline__ float pow2_scale(float var) {
+    float v = __fadd_rn(var, 1e-9f);
+    float s = 1.0f;
+    if (v >= 4.0f) s = 0.5f;
+    if (v >= 16.0f) s = 0.25f;
+    if (v >= 64.0f) s = 0.125f;
+    if (v >= 256.0f) s = 0.0625f;
+    if (v >= 1024.0f) s = 0.03125f;
+    if (v >= 4096.0f) s = 0.015625f;
+    if (v >= 16384.0f) s = 0.0078125f;
+    if (v >= 65536.0f) s = 0.00390625f;
+    if (v < 1.0f) s = 1.0f;
+    if (v < 0.25f) s = 2.0f;
+    if (v < 0.0625f) s = 4.0f;
+    if (v < 0.015625f) s = 8.0f;
+    return s;
+}
+
+// int8 value of clamp(ste_round(v), -127, 127), ste_round(v) = v + (rne(v) - v)
+// (src/rational_bitnet.py:54-60, :109)
+__device__ __forceinline__ int quant_i8(float v) {
+    float r = rintf(v);
+    float q = __fadd_rn(v, __fsub_rn(r, v));
+    q = clamp_t(q, -127.0f, 127.0f);
+    return (int)q;
+}
+
+// ceil(a / b) for positive ints
+__host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+}  // namespace mi
+
+#define MI_CHECK_LAUNCH()                                   \
+    do {                                                    \
+        cudaError_t e_ = cudaGetLastError();                \
+        if (e_ != cudaSuccess) return MI_ERR_CUDA;          \
+    } while (0)

@@ -1,0 +1,236 @@
+"""torch-tensor wrappers over the C ABI (one function per kernel entry point).
+
+Every wrapper checks devices/dtypes/contiguity, allocates its outputs with
+torch (the C ABI never allocates), launches on the current CUDA stream and
+raises on a non-zero status.  The names the reference's model imports from
+its Triton package are provided as aliases at the bottom
+(src/triton_kernels/bitnet_kernels.py:98, :295; dyadic_scan.py:462;
+fused_activations.py:229, :399, :511).
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype, name: str, contiguous: bool = True):
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (there is no CPU path)")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _scalar_dev(v, like: torch.Tensor) -> torch.Tensor:
+    if isinstance(v, torch.Tensor):
+        return v.to(device=like.device, dtype=torch.float32).reshape(1).contiguous()
+    return torch.tensor([float(v)], dtype=torch.float32, device=like.device)
+
+
+# ---------------------------------------------------------------------------
+# integer dyadic scan
+# ---------------------------------------------------------------------------
+def scan_i32(x: torch.Tensor, B: torch.Tensor, C: torch.Tensor, n: torch.Tensor, k: int = 15,
+             h0: Optional[torch.Tensor] = None, y_dtype=torch.int32, check_errors: bool = True
+             ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Integer selective scan; returns (y [b,L,D] y_dtype, h_T [b,D,N] int32)."""
+    for t, nm in ((x, "x"), (B, "B"), (C, "C"), (n, "n")):
+        _need(t, torch.int32, nm)
+    bsz, L, D = x.shape
+    N = n.shape[1]
+    if B.shape != (bsz, L, N) or C.shape != (bsz, L, N) or n.shape != (D, N):
+        raise ValueError("shape mismatch between x, B, C and n")
+    h = torch.zeros(bsz, D, N, dtype=torch.int32, device=x.device) if h0 is None else h0.clone()
+    _need(h, torch.int32, "h0")
+    y = torch.empty(bsz, L, D, dtype=y_dtype, device=x.device)
+    y32 = y if y_dtype == torch.int32 else None
+    y64 = y if y_dtype == torch.int64 else None
+    if y32 is None and y64 is None:
+        raise TypeError("y_dtype must be torch.int32 or torch.int64")
+    lib = _lib.load()
+    _lib.check(lib.mi_scan_i32(x.data_ptr(), B.data_ptr(), C.data_ptr(), n.data_ptr(), int(k), _ptr(y32), _ptr(y64),
+                               h.data_ptr(), bsz, L, D, N, _stream()), "mi_scan_i32")
+    if check_errors:
+        err = _lib.device_error(_stream())
+        if err:
+            raise OverflowError(f"integer scan device error word {err:#x} "
+                                "(1 = int32 overflow, 4 = input outside the stated range)")
+    return y, h
+
+
+# ---------------------------------------------------------------------------
+# row stages
+# ---------------------------------------------------------------------------
+def bitshift_norm(x: torch.Tensor, gamma: torch.Tensor, step, center_once: bool = False
+                  ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """BitShiftNorm forward (reference CPU semantics): returns (y, inv_rms[rows]).
+    center_once gives BitShiftNormFunction.forward alone (its input already centred once)."""
+    _need(x, torch.float32, "x")
+    D = x.shape[-1]
+    T = x.numel() // D
+    y = torch.empty_like(x)
+    inv = torch.empty(T, dtype=torch.float32, device=x.device)
+    g = gamma.detach().to(torch.float32).contiguous()
+    s = _scalar_dev(step, x)
+    _lib.check(_lib.load().mi_bitshift_norm(x.data_ptr(), g.data_ptr(), s.data_ptr(), y.data_ptr(), inv.data_ptr(),
+                                            T, D, int(center_once), _stream()), "mi_bitshift_norm")
+    return y, inv
+
+
+def quantize_rows(x: torch.Tensor, K: Optional[int] = None, out: Optional[torch.Tensor] = None,
+                  xscale: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-row absmax int8 quantisation of the first K columns of a 2-D fp32
+    tensor (row stride taken from x); returns (xq int8 [T, ldq], x_scale [T])."""
+    if x.dim() != 2 or x.stride(1) != 1:
+        raise ValueError("x must be 2-D with unit column stride")
+    _need(x, torch.float32, "x", contiguous=False)
+    T, W = x.shape
+    K = W if K is None else K
+    if out is None:
+        out = torch.empty(T, K, dtype=torch.int8, device=x.device)
+    if xscale is None:
+        xscale = torch.empty(T, dtype=torch.float32, device=x.device)
+    _lib.check(_lib.load().mi_quantize_rows(x.data_ptr(), x.stride(0), T, K, out.data_ptr(), out.stride(0),
+                                            xscale.data_ptr(), _stream()), "mi_quantize_rows")
+    return out, xscale
+
+
+def quantize_activations(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """activation_quant_dynamic: returns (xq as fp32 integer values [..., K],
+    scale / 127 [..., 1]) like the reference."""
+    K = x.shape[-1]
+    q, s = quantize_rows(x.contiguous().view(-1, K))
+    return q.to(torch.float32).view_as(x), s.view(*x.shape[:-1], 1)
+
+
+def rowprep(gamma, step, T: int, D: int, x=None, delta=None, res_gate=None, ids=None, emb=None, x_out=None,
+            y_norm=None, xq=None, xscale=None) -> None:
+    """Fused residual update + BitShiftNorm + int8 quantisation (see mi_rowprep)."""
+    vocab = emb.shape[0] if emb is not None else 0
+    _lib.check(_lib.load().mi_rowprep(_ptr(x), _ptr(delta), _ptr(res_gate), _ptr(ids), _ptr(emb), vocab, _ptr(x_out),
+                                      gamma.data_ptr(), step.data_ptr(), _ptr(y_norm), _ptr(xq), _ptr(xscale), T, D,
+                                      _stream()), "mi_rowprep")
+
+
+# ---------------------------------------------------------------------------
+# BitLinear GEMM
+# ---------------------------------------------------------------------------
+def bitlinear_i8(A: torch.Tensor, W: torch.Tensor, a_scale: Optional[torch.Tensor] = None,
+                 w_scale: Optional[torch.Tensor] = None, out_scale: Optional[torch.Tensor] = None,
+                 out: Optional[torch.Tensor] = None, K: Optional[int] = None) -> torch.Tensor:
+    """tcgen05 int8 GEMM: A int8 [M, >=K] (row stride from A), W int8 [N, K].
+    With a_scale/w_scale: fp32 acc * (w_scale * a_scale[m]) [* out_scale];
+    without: the int32 accumulators."""
+    _need(W, torch.int8, "W")
+    if A.dim() != 2 or A.stride(1) != 1:
+        raise ValueError("A must be 2-D with unit column stride")
+    _need(A, torch.int8, "A", contiguous=False)
+    M = A.shape[0]
+    N, Kw = W.shape
+    K = Kw if K is None else K
+    scaled = a_scale is not None
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32 if scaled else torch.int32, device=A.device)
+    epi = _lib.MI_EPI_F32_SCALED if scaled else _lib.MI_EPI_I32
+    _lib.check(_lib.load().mi_bitlinear_i8(A.data_ptr(), A.stride(0), W.data_ptr(), _ptr(a_scale), _ptr(w_scale),
+                                           _ptr(out_scale), out.data_ptr(), out.stride(0), M, N, K, epi, _stream()),
+               "mi_bitlinear_i8")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# conv / scan / element-wise
+# ---------------------------------------------------------------------------
+def conv_act_quant(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, batch: int, L: int, D: int,
+                   act=None, xq=None, xscale=None, quantize: bool = True):
+    """Causal depthwise conv + ste_clamp + squareplus (+ int8 quantisation) of
+    the first D columns of xz [batch*L, ldx]."""
+    T = batch * L
+    if act is None:
+        act = torch.empty(T, D, dtype=torch.float32, device=xz.device)
+    if quantize:
+        if xq is None:
+            xq = torch.empty(T, D, dtype=torch.int8, device=xz.device)
+        if xscale is None:
+            xscale = torch.empty(T, dtype=torch.float32, device=xz.device)
+    wc = w.detach().to(torch.float32).reshape(D, 4).contiguous()
+    bc = bias.detach().to(torch.float32).contiguous()
+    _lib.check(_lib.load().mi_conv_act_quant(xz.data_ptr(), xz.stride(0), wc.data_ptr(), bc.data_ptr(),
+                                             act.data_ptr(), _ptr(xq), _ptr(xscale), batch, L, D, _stream()),
+               "mi_conv_act_quant")
+    return act, xq, xscale
+
+
+def ssm_scan(act, bc, modraw, z, base, batch: int, L: int, y=None, amax=None):
+    """Fused selective scan + gate (see mi_ssm_scan).  bc / z may be column
+    slices (row stride taken from the tensor)."""
+    D, N = base.shape
+    T = batch * L
+    if y is None:
+        y = torch.empty(T, D, dtype=torch.float32, device=act.device)
+    _lib.check(_lib.load().mi_ssm_scan(act.data_ptr(), bc.data_ptr(), bc.stride(0), modraw.data_ptr(), z.data_ptr(),
+                                       z.stride(0), base.data_ptr(), y.data_ptr(), _ptr(amax), batch, L, D, N,
+                                       _stream()), "mi_ssm_scan")
+    return y
+
+
+def scan_convex(u: torch.Tensor, nums: torch.Tensor) -> torch.Tensor:
+    _need(u, torch.float32, "u")
+    _need(nums, torch.float32, "nums")
+    b, L, DN = u.shape
+    h = torch.empty_like(u)
+    _lib.check(_lib.load().mi_scan_convex(u.data_ptr(), nums.data_ptr(), h.data_ptr(), b, L, DN, _stream()),
+               "mi_scan_convex")
+    return h
+
+
+def squareplus_clamp(x: torch.Tensor, low: float = -50.0, high: float = 50.0) -> torch.Tensor:
+    _need(x, torch.float32, "x")
+    y = torch.empty_like(x)
+    _lib.check(_lib.load().mi_squareplus_clamp(x.data_ptr(), y.data_ptr(), x.numel(), low, high, _stream()),
+               "mi_squareplus_clamp")
+    return y
+
+
+def ste_clamp(x: torch.Tensor, low: float, high: float) -> torch.Tensor:
+    _need(x, torch.float32, "x")
+    y = torch.empty_like(x)
+    _lib.check(_lib.load().mi_ste_clamp(x.data_ptr(), y.data_ptr(), x.numel(), low, high, _stream()), "mi_ste_clamp")
+    return y
+
+
+def sigmoid_gate(y: torch.Tensor, z: torch.Tensor) -> torch.Tensor:
+    _need(y, torch.float32, "y")
+    _need(z, torch.float32, "z")
+    o = torch.empty_like(y)
+    _lib.check(_lib.load().mi_sigmoid_gate(y.data_ptr(), z.data_ptr(), o.data_ptr(), y.numel(), _stream()),
+               "mi_sigmoid_gate")
+    return o
+
+
+# Names used by the reference model for its GPU kernels.
+def fast_bitshift_norm(x, gamma, step_size=None):
+    step = torch.ones(1, device=x.device) if step_size is None else step_size
+    return bitshift_norm(x.contiguous(), gamma, step)
+
+
+fast_quantize_activations = quantize_activations
+fused_squareplus_clamp = squareplus_clamp
+fused_ste_clamp = ste_clamp
+fused_sigmoid_gate = sigmoid_gate
+
+
+def dyadic_scan_triton_fast(u, nums):
+    return scan_convex(u.contiguous(), nums.contiguous())

@@ -54,7 +54,7 @@ def _bitlinear(xf, wq_ws, nthreads, cap, name):
     if cap is not None:
         cap[name + ".xq"] = xq.reshape(-1, xq.shape[-1])
         cap[name + ".xscale"] = xs
-        cap[name + ".out"] = out
+        cap[name + ".out"] = out.copy()
     return out
 
 

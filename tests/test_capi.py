@@ -1,0 +1,49 @@
+"""The C-ABI library loads without a GPU and exports every entry point that
+include/*.h declares; the ctypes signature table covers exactly that set."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        names |= set(re.findall(r"^\s*(?:const\s+)?\w+\s*\**\s*(mi_\w+)\s*\(", src, flags=re.M))
+    return names
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from mamba_integer_b200 import build, _lib
+    build.build()
+    return _lib.load()
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert {"mi_scan_i32", "mi_bitlinear_i8", "mi_rowprep", "mi_ssm_scan", "mi_conv_act_quant"} <= names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    missing = [n for n in sorted(declared_symbols()) if not hasattr(lib, n)]
+    assert not missing, f"not exported: {missing}"
+
+
+def test_signature_table_matches_header():
+    from mamba_integer_b200 import _lib
+    assert set(_lib.SIGNATURES) == declared_symbols()
+
+
+def test_host_side_argument_errors_need_no_gpu(lib):
+    # rejected on the host before any CUDA call
+    assert lib.mi_scan_i32(None, None, None, None, 15, None, None, None, 1, 1, 16, 16, None) == -1
+    assert lib.mi_bitlinear_i8(None, 16, None, None, None, None, None, 16, 16, 16, 16, 0, None) == -1
+    assert lib.mi_version() >= 1
+    assert lib.mi_status_string(-2) == b"unsupported shape or configuration"

@@ -1,0 +1,230 @@
+"""GPU kernels against the CPU oracle, stage by stage, through the C ABI.
+Integer outputs must be identical; float stages too (the kernels replay the
+reference's floating-point order, so the tolerance is zero ulp)."""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import lib as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _mi():
+    from mamba_integer_b200 import _lib, kernels
+    _lib.load()
+    return kernels
+
+
+def _eq(a, b, what=""):
+    a = a.detach().cpu().numpy() if torch.is_tensor(a) else a
+    b = b.detach().cpu().numpy() if torch.is_tensor(b) else b
+    assert a.shape == b.shape, (what, a.shape, b.shape)
+    bad = a.view(np.uint8) != b.view(np.uint8) if a.dtype == b.dtype else a != b
+    if bad.any():
+        idx = np.argwhere(a != b)[:5]
+        raise AssertionError(f"{what}: {int((a != b).sum())} mismatches, first at {idx.tolist()}")
+
+
+# ---------------------------------------------------------------- integer scan
+@pytest.mark.parametrize("bsz,L,D", [(2, 300, 200), (1, 33, 64), (3, 1, 4), (2, 4096, 128)])
+def test_scan_i32_matches_oracle(cuda_dev, bsz, L, D):
+    k = _mi()
+    g = torch.Generator().manual_seed(bsz * 1000 + L + D)
+    q = lambda *s: torch.round(torch.randn(*s, generator=g) * 32).clamp(-127, 127).to(torch.int32)  # noqa: E731
+    x, B, C = q(bsz, L, D), q(bsz, L, 16), q(bsz, L, 16)
+    n = torch.randint(29492, 32736, (D, 16), generator=g, dtype=torch.int32)
+    n[0, 0], n[0, 1] = 0, 32768  # decay 0 and decay 1 edges
+    h0 = torch.randint(-2 ** 20, 2 ** 20, (bsz, D, 16), generator=g, dtype=torch.int32)
+    y_ref, h_ref = orc.scan_i32(x.numpy(), B.numpy(), C.numpy(), n.numpy(), 15, h0=h0.numpy())
+    dv = [t.to(cuda_dev) for t in (x, B, C, n, h0)]
+    y64, h64 = k.scan_i32(*dv[:4], 15, h0=dv[4], y_dtype=torch.int64)
+    _eq(y64, y_ref, "y64")
+    _eq(h64, h_ref, "h")
+    if np.abs(y_ref).max() < 2 ** 31:
+        y32, h32 = k.scan_i32(*dv[:4], 15, h0=dv[4], y_dtype=torch.int32)
+        _eq(y32, y_ref.astype(np.int32), "y32")
+        _eq(h32, h_ref, "h32")
+
+
+def test_scan_i32_kat_negative_floor(cuda_dev):
+    """h = -1, n = 1, k = 15: (-1*1) >> 15 = -1 (floor), not 0 (truncation)."""
+    k = _mi()
+    x = torch.zeros(1, 3, 4, dtype=torch.int32)
+    B = torch.zeros(1, 3, 16, dtype=torch.int32)
+    C = torch.zeros(1, 3, 16, dtype=torch.int32)
+    C[..., 0] = 1
+    n = torch.ones(4, 16, dtype=torch.int32)
+    h0 = torch.full((1, 4, 16), -1, dtype=torch.int32)
+    y, h = k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), 15, h0=h0.to(cuda_dev), y_dtype=torch.int64)
+    assert (h.cpu() == -1).all() and (y.cpu() == -1).all()
+
+
+def test_scan_i32_overflow_is_reported(cuda_dev):
+    k = _mi()
+    x = torch.full((1, 2, 4), 127, dtype=torch.int32)
+    B = torch.full((1, 2, 16), 127, dtype=torch.int32)
+    C = torch.ones(1, 2, 16, dtype=torch.int32)
+    n = torch.full((4, 16), 32768, dtype=torch.int32)
+    h0 = torch.full((1, 4, 16), 2 ** 31 - 100, dtype=torch.int32)
+    with pytest.raises(OverflowError):
+        k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), 15, h0=h0.to(cuda_dev), y_dtype=torch.int64)
+    x[0, 0, 0] = 40000  # outside the stated input range
+    with pytest.raises(OverflowError):
+        k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), 15, y_dtype=torch.int64)
+
+
+# ---------------------------------------------------------------- row stages
+@pytest.mark.parametrize("D", [256, 768, 1024, 32, 96])
+def test_bitshift_norm_matches_oracle(cuda_dev, D):
+    k = _mi()
+    g = torch.Generator().manual_seed(D)
+    x = torch.randn(333, D, generator=g) * torch.logspace(-3, 2.5, 333).unsqueeze(1) + torch.randn(333, 1, generator=g)
+    gamma = 1 + 0.1 * torch.randn(D, generator=g)
+    step = torch.tensor([0.875])
+    y_ref, inv_ref = orc.bitshift_norm(x.numpy(), gamma.numpy(), 0.875)
+    y, inv = k.bitshift_norm(x.to(cuda_dev), gamma.to(cuda_dev), step.to(cuda_dev))
+    _eq(y, y_ref, "norm y")
+    _eq(inv, inv_ref, "inv_rms")
+
+
+def test_norm_fixture_inputs(cuda_dev):
+    k = _mi()
+    x, g, st = cases.norm_inputs()
+    gold = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "stages.npz"))
+    y, inv = k.bitshift_norm(torch.from_numpy(x).to(cuda_dev), torch.from_numpy(g).to(cuda_dev),
+                             torch.from_numpy(st).to(cuda_dev))
+    _eq(y, gold["norm.y"], "norm y vs reference fixture")
+    _eq(inv, gold["norm.inv_rms"], "inv_rms vs reference fixture")
+
+
+@pytest.mark.parametrize("K", [256, 48, 1536, 80])
+def test_quantize_rows_matches_oracle(cuda_dev, K):
+    k = _mi()
+    x = cases.quant_inputs()[:, :K] if K <= 256 else np.random.default_rng(K).standard_normal((77, K)).astype(np.float32)
+    x = np.ascontiguousarray(x)
+    q_ref, s_ref = orc.quant_rows(x)
+    q, s = k.quantize_rows(torch.from_numpy(x).to(cuda_dev))
+    _eq(q, q_ref, "xq")
+    _eq(s, s_ref, "xscale")
+
+
+@pytest.mark.parametrize("D", [256, 768])
+def test_rowprep_fused_matches_oracle(cuda_dev, D):
+    k = _mi()
+    g = torch.Generator().manual_seed(7 + D)
+    T = 515
+    res = torch.randn(T, D, generator=g) * 3
+    out = torch.randn(T, D, generator=g)
+    gate = torch.tensor([0.144337567])
+    gamma = 1 + 0.05 * torch.randn(D, generator=g)
+    step = torch.tensor([1.0625])
+    newres = orc.residual(res.numpy(), out.numpy(), gate.numpy()[0])
+    y_ref, _ = orc.bitshift_norm(newres, gamma.numpy(), 1.0625)
+    q_ref, s_ref = orc.quant_rows(y_ref)
+    dv = lambda t: t.to(cuda_dev).contiguous()  # noqa: E731
+    xo = torch.empty(T, D, device=cuda_dev)
+    yn = torch.empty(T, D, device=cuda_dev)
+    xq = torch.empty(T, D, dtype=torch.int8, device=cuda_dev)
+    xs = torch.empty(T, device=cuda_dev)
+    k.rowprep(dv(gamma), dv(step), T, D, x=dv(res), delta=dv(out), res_gate=dv(gate), x_out=xo, y_norm=yn, xq=xq,
+              xscale=xs)
+    _eq(xo, newres, "residual")
+    _eq(yn, y_ref, "norm")
+    _eq(xq, q_ref, "xq")
+    _eq(xs, s_ref, "xscale")
+    # embedding-gather variant
+    emb = torch.randn(1000, D, generator=g)
+    ids = torch.randint(0, 1000, (T,), generator=g)
+    y2, _ = orc.bitshift_norm(emb.numpy()[ids.numpy()], gamma.numpy(), 1.0625)
+    q2, s2 = orc.quant_rows(y2)
+    k.rowprep(dv(gamma), dv(step), T, D, ids=dv(ids), emb=dv(emb), x_out=xo, xq=xq, xscale=xs)
+    _eq(xo, emb.numpy()[ids.numpy()], "gather")
+    _eq(xq, q2, "xq gather")
+    _eq(xs, s2, "xscale gather")
+
+
+# ---------------------------------------------------------------- GEMM
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (300, 3072, 768), (1000, 80, 1536), (257, 1536, 48),
+                                   (640, 768, 1536), (129, 4096, 256), (512, 96, 64)])
+def test_gemm_i8_matches_oracle(cuda_dev, M, N, K):
+    k = _mi()
+    g = torch.Generator().manual_seed(M * 7 + N * 3 + K)
+    A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    W = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8)
+    ref = orc.gemm_i8_i32(A.numpy(), W.numpy())
+    acc = k.bitlinear_i8(A.to(cuda_dev), W.to(cuda_dev))
+    _eq(acc, ref, "int32 accumulators")
+    xs = (torch.rand(M, generator=g) * 0.05 + 1e-3)
+    ws = torch.tensor([2.0 ** -6])
+    out_ref = orc.bitlinear(A.numpy(), xs.numpy(), W.numpy(), 2.0 ** -6)
+    out = k.bitlinear_i8(A.to(cuda_dev), W.to(cuda_dev), xs.to(cuda_dev), ws.to(cuda_dev))
+    _eq(out, out_ref, "scaled fp32")
+    os_ = torch.tensor([np.float32(1 / np.sqrt(768))])
+    out2 = k.bitlinear_i8(A.to(cuda_dev), W.to(cuda_dev), xs.to(cuda_dev), ws.to(cuda_dev), out_scale=os_.to(cuda_dev))
+    _eq(out2, (out_ref * os_.numpy()[0]).astype(np.float32), "output scale")
+
+
+def test_gemm_config3_slice(cuda_dev):
+    """BitLinear config 3 inputs (activation quant of N(0,1), ternary W): a 1024-row slice."""
+    from mamba_integer_b200 import synth
+    k = _mi()
+    A, a_scale, Wq, ws = synth.bitlinear_inputs(M=1024, K=2048, N=1024)
+    ref = orc.gemm_i8_i32(A.numpy(), Wq.numpy())
+    _eq(k.bitlinear_i8(A.to(cuda_dev), Wq.to(cuda_dev)), ref, "config-3 slice")
+
+
+# ---------------------------------------------------------------- conv / ssm / element-wise
+@pytest.mark.parametrize("bsz,L,D", [(2, 37, 512), (1, 130, 1536)])
+def test_conv_act_quant_matches_oracle(cuda_dev, bsz, L, D):
+    k = _mi()
+    g = torch.Generator().manual_seed(L + D)
+    xz = torch.randn(bsz * L, 2 * D, generator=g) * 20
+    w = torch.rand(D, 1, 4, generator=g) - 0.5
+    b = torch.rand(D, generator=g) - 0.5
+    _, act_ref = orc.conv_sqp(xz[:, :D].reshape(bsz, L, D).numpy(), w.numpy(), b.numpy())
+    act_ref = act_ref.reshape(bsz * L, D)
+    q_ref, s_ref = orc.quant_rows(act_ref)
+    act, xq, xs = k.conv_act_quant(xz.to(cuda_dev), w.to(cuda_dev), b.to(cuda_dev), bsz, L, D)
+    _eq(act, act_ref, "act")
+    _eq(xq, q_ref, "xq")
+    _eq(xs, s_ref, "xscale")
+
+
+@pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (3, 5, 160, 16)])
+def test_ssm_scan_matches_oracle(cuda_dev, bsz, L, D, R):
+    k = _mi()
+    g = torch.Generator().manual_seed(bsz + L + D)
+    T = bsz * L
+    act = torch.rand(T, D, generator=g) * 5
+    xp = torch.randn(T, R + 32, generator=g) * 2
+    modraw = torch.randn(T, D, generator=g) * 15
+    modraw[::7, ::5] = 1e9  # ste_clamp rounding edge
+    z = torch.randn(T, 2 * D, generator=g) * 3
+    base = torch.randint(29492, 32736, (D, 16), generator=g).float()
+    base[0, :] = 31990.0  # base + mod crosses 32000
+    base[1, :] = 5.0      # base + mod crosses 0
+    y_ref = orc.ssm(act.numpy(), np.ascontiguousarray(xp[:, R:].numpy()), modraw.numpy(),
+                    np.ascontiguousarray(z[:, D:].numpy()), base.numpy(), bsz, L)
+    dv = lambda t: t.to(cuda_dev)  # noqa: E731
+    xpd, zd = dv(xp), dv(z)
+    y = k.ssm_scan(dv(act), xpd[:, R:], dv(modraw), zd[:, D:], dv(base), bsz, L)
+    _eq(y, y_ref, "ssm y")
+
+
+def test_scan_convex_and_elementwise_match_reference_fixtures(cuda_dev):
+    import os
+    k = _mi()
+    gold = np.load(os.path.join(os.path.dirname(__file__), "golden", "stages.npz"))
+    u, nums = cases.scan_inputs()
+    _eq(k.scan_convex(torch.from_numpy(u).to(cuda_dev), torch.from_numpy(nums).to(cuda_dev)), gold["scan.h"], "scan")
+    e = torch.from_numpy(cases.edge_values()).to(cuda_dev)
+    _eq(k.squareplus_clamp(e, -50.0, 50.0), gold["sqp.y"], "squareplus")
+    _eq(k.ste_clamp(e, -20.0, 20.0), gold["ste20.y"], "ste_clamp")
+    _eq(k.ste_clamp(e, 0.0, 32000.0), gold["ste_dec.y"], "ste_clamp decay")
+    y, z = cases.gate_inputs()
+    _eq(k.sigmoid_gate(torch.from_numpy(y).to(cuda_dev), torch.from_numpy(z).to(cuda_dev)), gold["gate.y"], "gate")
+    q, s = k.quantize_rows(torch.from_numpy(cases.quant_inputs()).to(cuda_dev))
+    _eq(q, gold["quant.xq"], "quant")
+    _eq(s, gold["quant.scale"], "quant scale")
