@@ -152,7 +152,7 @@ def cpu_baseline(n_tokens: int = 256, threads: int = 0):
     sd = synth.model_state_dict(cfg, synth.CONFIGS["c4"]["seed"])
     p = om.prepare(sd)
     ids = synth.input_ids("c4", GLOBAL_BATCH, SEQ_LEN)[:1, :n_tokens].numpy()
-    om.forward(p, cfg, ids[:, :16], nthreads=threads)  # warm
+    om.forward(p, cfg, ids[:, :16], nthreads=threads)  # warm-up (page in the weights)
     t0 = time.perf_counter()
     om.forward(p, cfg, ids, nthreads=threads)
     dt = time.perf_counter() - t0
@@ -196,6 +196,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # smaller shapes for profiling captures only (the reported workload is 64 x 2048)
+    ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
+    ap.add_argument("--seq", type=int, default=SEQ_LEN)
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -225,16 +228,17 @@ def main():
     model.load_state_dict(sd)
     model = model.to(dev).eval()
     eng = model.engine()
-    ids_all = synth.input_ids("c4", GLOBAL_BATCH, SEQ_LEN)
-    per = GLOBAL_BATCH // world
+    gb, sl = args.batch, args.seq
+    ids_all = synth.input_ids("c4", gb, sl)
+    per = gb // world
     lo = rank * per
-    hi = GLOBAL_BATCH if rank == world - 1 else lo + per
+    hi = gb if rank == world - 1 else lo + per
     ids_host = ids_all[lo:hi].contiguous().pin_memory()
     ids_dev = ids_host.to(dev)
     b_local = hi - lo
-    T_local = b_local * SEQ_LEN
+    T_local = b_local * sl
     V = cfg["vocab_size"]
-    logits = torch.empty(b_local, SEQ_LEN, V, dtype=torch.float32, device=dev)
+    logits = torch.empty(b_local, sl, V, dtype=torch.float32, device=dev)
     gathered = torch.empty(per * world, V, dtype=torch.float32, device=dev) if world > 1 else None
     last_local = torch.empty(per, V, dtype=torch.float32, device=dev)
 
@@ -266,7 +270,7 @@ def main():
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-        value = GLOBAL_BATCH * SEQ_LEN * args.steps / (ms / 1000.0)
+        value = gb * sl * args.steps / (ms / 1000.0)
 
         # end to end through the public API: pinned host ids -> device, forward,
         # last-position logits -> pinned host
@@ -285,7 +289,7 @@ def main():
         ems = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
         if world > 1:
             dist.all_reduce(ems, op=dist.ReduceOp.MAX)
-        e2e_val = GLOBAL_BATCH * SEQ_LEN * e2e_steps / (float(ems.item()) / 1000.0)
+        e2e_val = gb * sl * e2e_steps / (float(ems.item()) / 1000.0)
 
         # per-kernel CUDA-event timing of one more forward (outside the timed region)
         tim = EventTimer()
@@ -312,7 +316,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cores = os.cpu_count() or 1
-        n_tok = int(os.environ.get("MI_CPU_SAMPLE_TOKENS", "128"))
+        n_tok = int(os.environ.get("MI_CPU_SAMPLE_TOKENS", "2048"))
         v_cpu, dt_cpu, _, _ = cpu_baseline(n_tok, cores)
         cpu = {"value": v_cpu, "unit": UNIT, "cores": cores, "kind": "port",
                "sample": f"1 sequence x {n_tok} tokens of config 4 (24 layers + lm_head), oracle C port, "
@@ -323,7 +327,8 @@ def main():
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32+int8", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": GLOBAL_BATCH, "seq_len": SEQ_LEN,
+            "config": {"workload": WORKLOAD if (gb, sl) == (GLOBAL_BATCH, SEQ_LEN) else f"profiling_b{gb}x{sl}",
+                       "global_batch": gb, "seq_len": sl,
                        "parallelism": f"batch split {world}" if world > 1 else "single GPU",
                        "l2": "working set (>= 1.6 GB per activation buffer) far larger than L2; no flush needed"},
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": int(ids_host.numel() * 8),

@@ -75,10 +75,12 @@ int mi_bitshift_norm(const float* x, const float* gamma, const float* step, floa
  *   s = max(amax|x|, 1e-8); xq = clamp(rne(x * (127 * (1/s))), +-127);
  *   xscale = s / 127.
  * x [T, >=K] row stride ldx; xq [T, >=K] row stride ldq (int8).
+ * amax (optional, [T]): max|x| of each row already computed by the producer
+ * of x (NULL: computed here).
  * Replaces: fast_quantize_activations, src/triton_kernels/bitnet_kernels.py:98.
  */
 int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
-                     void* stream);
+                     const float* amax, void* stream);
 
 /*
  * Row pre-pass in front of a BitLinear: optional residual update, BitShiftNorm,
@@ -118,12 +120,13 @@ int mi_bitlinear_i8(const int8_t* A, int lda, const int8_t* W, const float* a_sc
  * ste_clamp(-50, 50) + squareplus (3 Newton steps), then int8 quantisation of
  * each row of the activation.
  * xz rows [batch*L] with stride ldx: the first D columns are the conv input;
- * w [D,4], bias [D]; act [batch*L, D]; xq [batch*L, D]; xscale [batch*L].
+ * w [D,4], bias [D]; act [batch*L, D]; xq [batch*L, D]; xscale [batch*L];
+ * amax_ws: caller-provided workspace of batch*L floats (required with xq).
  * Replaces: conv1d + fused_squareplus_clamp, src/mamba_integer_model.py:404-411
  * (fused_squareplus_clamp: src/triton_kernels/fused_activations.py:229).
  */
 int mi_conv_act_quant(const float* xz, int ldx, const float* w, const float* bias, float* act,
-                      int8_t* xq, float* xscale, int batch, int L, int D, void* stream);
+                      int8_t* xq, float* xscale, float* amax_ws, int batch, int L, int D, void* stream);
 
 /*
  * Selective-scan section of MambaIntegerBlock from the dt_proj output on:
@@ -131,7 +134,8 @@ int mi_conv_act_quant(const float* xz, int ldx, const float* w, const float* bia
  * d = n/2^15, y = sum_n h*C (FMA, n ascending), gate y*sigmoid_alg(z).
  * act [batch*L, D]; bc rows (stride ldbc): B at [0,N), C at [N,2N);
  * modraw [batch*L, D]; z rows stride ldz; base [D,N]; y [batch*L, D].
- * amax (optional, [batch*L], zero-filled by the caller) receives max|y| per row.
+ * amax (optional, [batch*L], zero-filled by the caller) receives max|y| per row
+ * (feed it to mi_quantize_rows).
  * N == 16.
  * Replaces: DyadicScanFunction.apply / dyadic_scan_triton_fast
  * (src/mamba_integer_model.py:419-444, src/triton_kernels/dyadic_scan.py:462).

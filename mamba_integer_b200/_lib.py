@@ -30,10 +30,10 @@ SIGNATURES = {
     "mi_device_error": [ctypes.POINTER(ctypes.c_int), _i, _p],
     "mi_scan_i32": [_p, _p, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
     "mi_bitshift_norm": [_p, _p, _p, _p, _p, _i, _i, _i, _p],
-    "mi_quantize_rows": [_p, _i, _i, _i, _p, _i, _p, _p],
+    "mi_quantize_rows": [_p, _i, _i, _i, _p, _i, _p, _p, _p],
     "mi_rowprep": [_p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mi_bitlinear_i8": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
-    "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
+    "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_ssm_scan": [_p, _p, _i, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
     "mi_scan_convex": [_p, _p, _p, _i, _i, _i, _p],
     "mi_squareplus_clamp": [_p, _p, _i64, _f, _f, _p],

@@ -3,15 +3,18 @@
 // ternary weights stored as int8, tcgen05.mma kind::i8 with int32
 // accumulators in tensor memory.
 //
-// Per CTA one BM x BN output tile (BM = 128 rows of tokens):
+// Persistent, one CTA per SM, BM x BN output tiles (BM = 128 rows of tokens):
 //   warp 0 / lane 0  TMA producer: 2-D tiled loads (128-byte swizzle) of the
 //                    A and W K-slices into a STAGES-deep shared-memory ring;
 //   warp 1 / lane 0  MMA issuer: 4 x tcgen05.mma (K = 32 bytes each) per
-//                    128-byte K-slice, tcgen05.commit frees the slot;
-//   all 4 warps      epilogue: tcgen05.ld 32x32b (one accumulator row per
+//                    128-byte K-slice into one of two TMEM accumulators,
+//                    tcgen05.commit frees the ring slot / hands the
+//                    accumulator to the epilogue;
+//   warps 2-5        epilogue: tcgen05.ld 32x32b (one accumulator row per
 //                    thread), dequantise acc * (w_scale * a_scale[m])
 //                    [* out_scale] exactly as BitLinear.forward does
-//                    (src/rational_bitnet.py:204-208), store.
+//                    (src/rational_bitnet.py:204-208), stage 32x32 boxes in
+//                    swizzled shared memory, TMA bulk tensor store.
 // Every mbarrier wait is bounded (about 2 s of clock); on expiry the CTA sets
 // MI_DEV_TIMEOUT, stops issuing, frees its tensor memory and exits.
 //
@@ -27,20 +30,25 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage: one 128-byte swizzle row
-constexpr int THREADS = 128;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // producer warp, MMA warp, 4 epilogue warps
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 
 template <int BN>
 struct Cfg {
-    static constexpr int STAGES = BN >= 256 ? 4 : (BN >= 128 ? 3 : 4);
+    static constexpr int STAGES = 4;
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+    static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per accumulator
+    static constexpr int EPI_BOXES = (BN + 31) / 32;   // 32-column output boxes per tile
+    static constexpr int STG_BYTES = EPI_WARPS * 2 * 4096;  // two staging boxes per epilogue warp
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the 128B swizzle");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
+    static_assert(2 * TMEM_COLS <= 512, "two accumulators must fit in TMEM");
+    static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -81,6 +89,12 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm,
             dst),
         "l"((uint64_t)tm), "r"(bar), "r"(x), "r"(y)
         : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"((uint64_t)tm),
+                 "r"(src), "r"(x), "r"(y)
+                 : "memory");
 }
 
 // Shared-memory matrix descriptor, K-major operand in the canonical 128-byte
@@ -129,42 +143,53 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+// Persistent kernel: each CTA walks the output tiles blockIdx.x,
+// blockIdx.x + gridDim.x, ... (N fastest, so CTAs working at the same time
+// share the A row-block in L2).  The smem ring and the two TMEM accumulators
+// carry across tiles, so the epilogue of tile i overlaps the mainloop of
+// tile i+1.
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const float* __restrict__ a_scale, const float* __restrict__ w_scale,
-               const float* __restrict__ out_scale, void* __restrict__ out, int ldo, int M, int N, int K, int epi) {
+               const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
+               const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K, int epi) {
     using C = Cfg<BN>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-aligned tiles
     unsigned char* gbase = smem_raw + (base - raw);
-    const uint32_t bars = base + C::STAGES * C::STAGE_BYTES;
-    // barrier block: full[S], empty[S], accum, then tmem slot and abort flag
+    const uint32_t stg_base = base + C::STAGES * C::STAGE_BYTES;  // epilogue staging (1024-aligned)
+    const uint32_t bars = stg_base + C::STG_BYTES;
+    // barriers: full[S], empty[S], tfull[2], tempty[2]; then the TMEM slot and the abort flag
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
-    const uint32_t accum_bar = bars + 8u * (2 * C::STAGES);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::STAGES * C::STAGE_BYTES + 8 * (2 * C::STAGES + 1));
+    auto tfull_bar = [&](int a) { return bars + 8u * (2 * C::STAGES + a); };
+    auto tempty_bar = [&](int a) { return bars + 8u * (2 * C::STAGES + 2 + a); };
+    uint32_t* tmem_slot =
+        reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * C::STAGES + 4));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * BM;
     const int num_k = cdiv(K, BK);
+    const int tiles_n = cdiv(N, BN);
+    const int num_tiles = cdiv(M, BM) * tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; s++) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
-        mbar_init(accum_bar, 1);
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), EPI_WARPS);
+        }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
-                     "r"((uint32_t)C::TMEM_COLS)
+                     "r"((uint32_t)(2 * C::TMEM_COLS))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
@@ -173,91 +198,134 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // ---------------- TMA producer ----------------
-        for (int i = 0; i < num_k; i++) {
-            const int s = i % C::STAGES;
-            if (i >= C::STAGES) {
-                if (!mbar_wait(empty_bar(s), ((i / C::STAGES) - 1) & 1, abort_flag)) break;
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int g = 0;  // global k-stage counter across tiles
+            for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+                const int m0 = (tile / tiles_n) * BM;
+                const int n0 = (tile % tiles_n) * BN;
+                for (int i = 0; i < num_k; i++, g++) {
+                    const int s = g % C::STAGES;
+                    if (g >= C::STAGES && !mbar_wait(empty_bar(s), ((g / C::STAGES) - 1) & 1, abort_flag)) break;
+                    const uint32_t sa = base + s * C::STAGE_BYTES;
+                    mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
+                    tma_load_2d(sa, &tmA, full_bar(s), i * BK, m0);
+                    tma_load_2d(sa + C::A_BYTES, &tmB, full_bar(s), i * BK, n0);
+                }
             }
-            const uint32_t sa = base + s * C::STAGE_BYTES;
-            mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
-            tma_load_2d(sa, &tmA, full_bar(s), i * BK, m0);
-            tma_load_2d(sa + C::A_BYTES, &tmB, full_bar(s), i * BK, n0);
+            if (*abort_flag) {
+                // let the loads already issued land before the CTA exits (bounded)
+                for (int j = (g > C::STAGES ? g - C::STAGES : 0); j < g; j++) {
+                    const long long t0 = clock64();
+                    while (!mbar_try(full_bar(j % C::STAGES), (j / C::STAGES) & 1) && clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
+            }
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
-        constexpr uint32_t idesc = idesc_i8<BN>();
-        bool ok = true;
-        for (int i = 0; i < num_k; i++) {
-            const int s = i % C::STAGES;
-            if (!mbar_wait(full_bar(s), (i / C::STAGES) & 1, abort_flag)) {
-                ok = false;
-                break;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_i8<BN>();
+            int g = 0;
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, it++) {
+                const int a = it & 1;
+                if (it >= 2 && !mbar_wait(tempty_bar(a), ((it >> 1) - 1) & 1, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t tacc = tmem + (uint32_t)(a * C::TMEM_COLS);
+                bool ok = true;
+                for (int i = 0; i < num_k; i++, g++) {
+                    const int s = g % C::STAGES;
+                    if (!mbar_wait(full_bar(s), (g / C::STAGES) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = base + s * C::STAGE_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; kk++) {
+                        const uint64_t ad = sdesc_sw128(sa + kk * 32);
+                        const uint64_t bd = sdesc_sw128(sa + C::A_BYTES + kk * 32);
+                        mma_i8(tacc, ad, bd, idesc, (i | kk) != 0);
+                    }
+                    mma_commit(empty_bar(s));
+                }
+                if (!ok) break;
+                mma_commit(tfull_bar(a));
             }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        // A warp may only touch the TMEM lane quarter warp % 4: it owns the tile
+        // rows q*32 .. q*32+31.  Each 32-column slab is dequantised, written in
+        // the 128-byte-swizzled layout of a 32x32 TMA box into one of two
+        // staging buffers, and stored with a bulk tensor copy (TMA clips rows
+        // >= M and columns >= N).
+        const int q = warp & 3;
+        const uint32_t stg = stg_base + (uint32_t)((warp - 2) * 2 * 4096);
+        unsigned char* stg_g = gbase + (stg - base);
+        const float ws = (epi == MI_EPI_F32_SCALED) ? *w_scale : 0.0f;
+        const float os = out_scale ? *out_scale : 1.0f;
+        int it = 0, nst = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, it++) {
+            const int a = it & 1;
+            const bool have = __all_sync(0xffffffffu, mbar_wait(tfull_bar(a), (it >> 1) & 1, abort_flag));
+            if (!have) break;
             tc_fence_after();
-            const uint32_t sa = base + s * C::STAGE_BYTES;
-#pragma unroll
-            for (int kk = 0; kk < BK / 32; kk++) {
-                const uint64_t ad = sdesc_sw128(sa + kk * 32);
-                const uint64_t bd = sdesc_sw128(sa + C::A_BYTES + kk * 32);
-                mma_i8(tmem, ad, bd, idesc, (i | kk) != 0);
-            }
-            mma_commit(empty_bar(s));
-        }
-        if (ok) mma_commit(accum_bar);
-    }
-    __syncwarp();
-
-    // ---------------- epilogue ----------------
-    const bool have = __all_sync(0xffffffffu, mbar_wait(accum_bar, 0, abort_flag));
-    tc_fence_after();
-    if (have) {
-        const int row = m0 + warp * 32 + lane;
-        const bool row_ok = row < M;
-        float sc = 0.0f, os = 1.0f;
-        if (epi == MI_EPI_F32_SCALED && row_ok) {
-            sc = __fmul_rn(*w_scale, a_scale[row]);  // (w_scale * x_scale)
-            if (out_scale) os = *out_scale;
-        }
+            const int m0 = (tile / tiles_n) * BM;
+            const int n0 = (tile % tiles_n) * BN;
+            const int row = m0 + q * 32 + lane;
+            float sc = 0.0f;
+            if (epi == MI_EPI_F32_SCALED && row < M) sc = __fmul_rn(ws, a_scale[row]);  // (w_scale * x_scale)
+            const uint32_t tacc = tmem + (uint32_t)(a * C::TMEM_COLS) + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-            uint32_t r[16];
-            tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, r);
-            const int col = n0 + c0;
-            if (!row_ok || col >= N) continue;
-            if (epi == MI_EPI_I32) {
-                int32_t* o = reinterpret_cast<int32_t*>(out) + (size_t)row * ldo + col;
-                if (col + 16 <= N) {
-#pragma unroll
-                    for (int j = 0; j < 16; j += 4)
-                        *reinterpret_cast<int4*>(o + j) = make_int4(r[j], r[j + 1], r[j + 2], r[j + 3]);
-                } else {
-                    for (int j = 0; j < 16 && col + j < N; j++) o[j] = (int32_t)r[j];
+            for (int cb = 0; cb < C::EPI_BOXES; cb++, nst++) {
+                uint32_t r[32] = {};
+                tmem_ld16(tacc + (uint32_t)(cb * 32), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                if (cb * 32 + 16 < BN)
+                    tmem_ld16(tacc + (uint32_t)(cb * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                if (cb == C::EPI_BOXES - 1) {
+                    // every TMEM read of this accumulator is done: hand it back to the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(tempty_bar(a)) : "memory");
                 }
-            } else {
-                float v[16];
+                if (epi == MI_EPI_F32_SCALED) {
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    v[j] = __fmul_rn((float)(int32_t)r[j], sc);
-                    if (out_scale) v[j] = __fmul_rn(v[j], os);
+                    for (int j = 0; j < 32; j++) {
+                        float v = __fmul_rn((float)(int32_t)r[j], sc);
+                        if (out_scale) v = __fmul_rn(v, os);
+                        r[j] = __float_as_uint(v);
+                    }
                 }
-                float* o = reinterpret_cast<float*>(out) + (size_t)row * ldo + col;
-                if (col + 16 <= N) {
+                // the staging buffer used two stores ago must have been read
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+                __syncwarp();
+                unsigned char* rowp = stg_g + (nst & 1) * 4096 + lane * 128;
 #pragma unroll
-                    for (int j = 0; j < 16; j += 4)
-                        *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                } else {
-                    for (int j = 0; j < 16 && col + j < N; j++) o[j] = v[j];
+                for (int c = 0; c < 8; c++) {
+                    const int phys = c ^ (lane & 7);
+                    *reinterpret_cast<uint4*>(rowp + phys * 16) =
+                        make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    const int x = n0 + cb * 32, y = m0 + q * 32;
+                    if (x < N && y < M) tma_store_2d(&tmC, stg + (nst & 1) * 4096, x, y);
+                    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
                 }
             }
         }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
-                     "r"((uint32_t)C::TMEM_COLS)
+                     "r"((uint32_t)(2 * C::TMEM_COLS))
                      : "memory");
     }
 }
@@ -277,15 +345,18 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
-// 2-D int8 tensor [rows, cols] with row pitch ld bytes; box = 128 bytes x box_rows.
-static int make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int ld, int box_rows) {
+// 2-D tensor [rows, cols] of `esize`-byte elements with row pitch ld_bytes;
+// box = box_cols x box_rows, 128-byte swizzle (box_cols * esize == 128).
+static int make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, long long ld_bytes, int box_cols,
+                     int box_rows, int esize) {
     auto enc = get_encode();
     if (!enc) return MI_ERR_CUDA;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)ld};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint64_t strides[1] = {(cuuint64_t)ld_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+    CUtensorMapDataType dt = esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
+    CUresult r = enc(tm, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MI_OK : MI_ERR_CUDA;
@@ -294,16 +365,28 @@ static int make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, int l
 template <int BN>
 static int launch(const int8_t* A, int lda, const int8_t* W, const float* a_scale, const float* w_scale,
                   const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
-    CUtensorMap ta, tb;
-    int rc = make_tmap(&ta, A, M, K, lda, BM);
+    // a tile whose last 32-column box sticks out past BN would overwrite the next tile
+    if ((BN % 32) != 0 && N > BN) return MI_ERR_UNSUPPORTED;
+    CUtensorMap ta, tb, tc;
+    int rc = make_tmap(&ta, A, M, K, lda, BK, BM, 1);
     if (rc) return rc;
-    rc = make_tmap(&tb, W, N, K, K, BN);
+    rc = make_tmap(&tb, W, N, K, K, BK, BN, 1);
+    if (rc) return rc;
+    rc = make_tmap(&tc, out, M, N, (long long)ldo * 4, 32, 32, 4);
     if (rc) return rc;
     using C = Cfg<BN>;
     if (cudaFuncSetAttribute(gemm_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
         return MI_ERR_CUDA;
-    dim3 grid(cdiv(N, BN), cdiv(M, BM));
-    gemm_i8_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, a_scale, w_scale, out_scale, out, ldo, M, N, K, epi);
+    static int num_sms = 0;
+    if (!num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (num_sms <= 0) num_sms = 148;
+    }
+    const int tiles = cdiv(M, BM) * cdiv(N, BN);
+    const int grid = tiles < num_sms ? tiles : num_sms;
+    gemm_i8_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M, N, K, epi);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

@@ -22,13 +22,22 @@ __device__ int g_dev_error;
 
 __device__ __forceinline__ void raise_dev_error(int bits) { atomicOr(&g_dev_error, bits); }
 
-// torch.clamp(x, lo, hi) on fp32: NaN propagates.
-__device__ __forceinline__ float clamp_t(float x, float lo, float hi) {
-    if (x != x) return x;
-    if (x < lo) return lo;
-    if (x > hi) return hi;
-    return x;
+// NaN-propagating min / max (PTX min.NaN / max.NaN), as torch.minimum/maximum.
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
 }
+__device__ __forceinline__ float min_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// torch.clamp(x, lo, hi) on fp32: NaN propagates.  (The sign of a zero result
+// can differ from ATen's, which never matters downstream: every clamp here is
+// followed by arithmetic that maps +-0 to the same value, or by an int cast.)
+__device__ __forceinline__ float clamp_t(float x, float lo, float hi) { return min_nan(max_nan(x, lo), hi); }
 
 // ste_clamp forward value x + (clamp(x) - x)  (src/mamba_integer_model.py:136-141)
 __device__ __forceinline__ float ste_clamp(float x, float lo, float hi) {
@@ -58,11 +67,31 @@ __device__ __forceinline__ float rsqrt_newton(float y) {
     return r;
 }
 
+// _rsqrt_newton for an argument known to be >= 4 or NaN (x*x + 4 always is):
+// the three "y < 4 / 1 / 0.25" entries of the guess table can never fire, so
+// they are skipped; every other operation is the same as rsqrt_newton.
+__device__ __forceinline__ float rsqrt_newton_ge4(float y) {
+    y = clamp_t(y, 1e-6f, 1e6f);
+    float r = (y > 16.0f) ? 0.125f : 0.5f;
+    r = (y > 64.0f) ? 0.0625f : r;
+    r = (y > 256.0f) ? 0.03125f : r;
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        float t = __fmul_rn(0.5f, y);
+        t = __fmul_rn(t, r);
+        t = __fmul_rn(t, r);
+        t = __fsub_rn(1.5f, t);
+        r = __fmul_rn(r, t);
+        r = clamp_t(r, 1e-6f, 1e3f);
+    }
+    return r;
+}
+
 // _squareplus_rational (src/mamba_integer_model.py:105-121)
 __device__ __forceinline__ float squareplus(float x) {
-    float ysq = __fadd_rn(__fmul_rn(x, x), 4.0f);
+    float ysq = __fadd_rn(__fmul_rn(x, x), 4.0f);  // >= 4 or NaN
     float ys = clamp_t(ysq, 1e-6f, 1e6f);
-    float r = rsqrt_newton(ys);
+    float r = rsqrt_newton_ge4(ys);
     float s = clamp_t(__fmul_rn(ys, r), 0.0f, 1e3f);
     return __fmul_rn(0.5f, __fadd_rn(x, s));
 }

@@ -157,19 +157,24 @@ rowprep_kernel(const float* x, const float* delta, const float* __restrict__ res
 // absmax, then quantise; the second pass re-reads the row from L1/L2).
 __global__ void __launch_bounds__(256)
 quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __restrict__ xq, int ldq,
-                  float* __restrict__ xscale) {
+                  float* __restrict__ xscale, const float* __restrict__ amax_in) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
         const float* row = x + (size_t)t * ldx;
-        float am = 0.0f;
-        bool nan = false;
-        for (int k = lane; k < K; k += 32) {
-            float a = fabsf(row[k]);
-            nan |= (a != a);
-            am = fmaxf(am, a);
+        float amax;
+        if (amax_in) {
+            amax = amax_in[t];  // max |x| of the row, produced by the kernel that wrote x
+        } else {
+            float am = 0.0f;
+            bool nan = false;
+            for (int k = lane; k < K; k += 32) {
+                float a = fabsf(row[k]);
+                nan |= (a != a);
+                am = fmaxf(am, a);
+            }
+            amax = warp_absmax(am, nan);
         }
-        float amax = warp_absmax(am, nan);
         float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
         float inv = __fmul_rn(__frcp_rn(sc), 127.0f);
         for (int k = lane; k < K; k += 32) xq[(size_t)t * ldq + k] = (int8_t)quant_i8(__fmul_rn(row[k], inv));
@@ -248,14 +253,14 @@ extern "C" int mi_rowprep(const float* x, const float* delta, const float* res_g
 }
 
 extern "C" int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
-                                void* stream) {
+                                const float* amax, void* stream) {
     if (!x || !xq || !xscale) return MI_ERR_INVALID;
     if (T < 0 || K <= 0 || ldx < K || ldq < K) return MI_ERR_INVALID;
     if (T == 0) return MI_OK;
     const int threads = 256;
     int blocks = mi::cdiv(T, threads / 32);
     if (blocks > 148 * 16) blocks = 148 * 16;
-    mi::rowops::quant_rows_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq, xscale);
+    mi::rowops::quant_rows_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq, xscale, amax);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

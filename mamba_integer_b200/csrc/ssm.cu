@@ -1,6 +1,7 @@
 // ssm.cu -- the selective-scan half of MambaIntegerBlock on sm_100a:
-//   * causal depthwise conv + ste_clamp + squareplus + int8 quantisation
-//     (feeds x_proj and the scan), one warp per token row;
+//   * causal depthwise conv + ste_clamp + squareplus (+ row absmax), one
+//     thread per (sequence, channel) walking the positions, then the int8
+//     quantisation that feeds x_proj;
 //   * the fused selective scan: decay clamp, dt, u = (x*dt)*B, the convex
 //     dyadic recurrence, y = sum_n h*C and the algebraic-sigmoid gate, one
 //     thread per (sequence, channel) carrying its 16 fp32 states in registers;
@@ -18,45 +19,66 @@ namespace ssm {
 // ---------------------------------------------------------------------------
 // conv + activation + quantisation
 // ---------------------------------------------------------------------------
-// xz: [batch*L, ldx], conv input = columns [0, D).  act/xq: [batch*L, D].
-__global__ void __launch_bounds__(256)
-conv_act_quant_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w,
-                      const float* __restrict__ bias, float* __restrict__ act, int8_t* __restrict__ xq,
-                      float* __restrict__ xscale, int L, int D, int T) {
+// One thread per (sequence, channel) walks a chunk of CONV_TC positions with the
+// 4-tap window in registers, so every input element is read once, coalesced
+// across channels.  The row absmax needed by the following int8 quantisation
+// is accumulated with one atomicMax per warp and position into amax (fp32
+// bits of non-negative values order like unsigned integers; NaN sorts above
+// +inf, which makes a NaN row propagate as torch.amax does).
+constexpr int CONV_THREADS = 128;
+constexpr int CONV_TC = 64;  // positions per CTA
+constexpr int CONV_G = 8;    // positions per group: computed together, absmax reduced together
+
+// xz: [batch*L, ldx], conv input = columns [0, D).  act: [batch*L, D].
+__global__ void __launch_bounds__(CONV_THREADS)
+conv_act_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w, const float* __restrict__ bias,
+                float* __restrict__ act, unsigned int* __restrict__ amax, int L, int D) {
+    const int c = blockIdx.x * CONV_THREADS + threadIdx.x;
     const int lane = threadIdx.x & 31;
-    const int warps = blockDim.x >> 5;
-    for (int row = blockIdx.x * warps + (threadIdx.x >> 5); row < T; row += gridDim.x * warps) {
-        const int t = row % L;  // position within its sequence
-        float am = 0.0f;
-        bool nan = false;
-        for (int c = lane; c < D; c += 32) {
-            const float4 wc = *reinterpret_cast<const float4*>(w + 4 * c);
-            const float wk[4] = {wc.x, wc.y, wc.z, wc.w};
-            float acc = bias[c];
+    const int b = blockIdx.y;
+    const int t0 = blockIdx.z * CONV_TC;
+    const bool active = c < D;
+    const int cc = active ? c : 0;
+    const float4 wc = *reinterpret_cast<const float4*>(w + 4 * cc);
+    const float bs = bias[cc];
+    const size_t row0 = (size_t)b * L;
+    const float* px = xz + row0 * ldx + cc;
+    // window x[t-3], x[t-2], x[t-1]
+    float w0 = (t0 - 3 >= 0) ? px[(size_t)(t0 - 3) * ldx] : 0.0f;
+    float w1 = (t0 - 2 >= 0) ? px[(size_t)(t0 - 2) * ldx] : 0.0f;
+    float w2 = (t0 - 1 >= 0) ? px[(size_t)(t0 - 1) * ldx] : 0.0f;
+    const int tend = min(L, t0 + CONV_TC);
+    for (int t = t0; t < tend; t += CONV_G) {
+        float xv[CONV_G];
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int dt = 3 - k;  // tap k reads position t - 3 + k
-                const float xv = (t - dt >= 0) ? xz[(size_t)(row - dt) * ldx + c] : 0.0f;
-                acc = __fmaf_rn(wk[k], xv, acc);
-            }
+        for (int j = 0; j < CONV_G; j++) xv[j] = (t + j < tend) ? __ldg(px + (size_t)(t + j) * ldx) : 0.0f;
+        unsigned m[CONV_G];
+#pragma unroll
+        for (int j = 0; j < CONV_G; j++) {
+            // bias first, then one FMA per tap k = 0..3 over positions t-3+k
+            float acc = bs;
+            acc = __fmaf_rn(wc.x, w0, acc);
+            acc = __fmaf_rn(wc.y, w1, acc);
+            acc = __fmaf_rn(wc.z, w2, acc);
+            acc = __fmaf_rn(wc.w, xv[j], acc);
+            w0 = w1;
+            w1 = w2;
+            w2 = xv[j];
             const float a = squareplus(ste_clamp(acc, -50.0f, 50.0f));
-            act[(size_t)row * D + c] = a;
-            const float aa = fabsf(a);
-            nan |= (aa != aa);
-            am = fmaxf(am, aa);
+            const bool ok = active && (t + j < tend);
+            if (ok) act[(row0 + t + j) * D + c] = a;
+            m[j] = ok ? __float_as_uint(fabsf(a)) : 0u;
         }
-        if (xq) {
+        // row absmax of the group's positions: butterflies interleaved over the group
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-            nan = __any_sync(0xffffffffu, nan);
-            const float amax = nan ? __int_as_float(0x7fc00000) : am;
-            const float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
-            const float inv = __fmul_rn(__frcp_rn(sc), 127.0f);
-            // each lane re-reads only the values it wrote itself
-            for (int c = lane; c < D; c += 32)
-                xq[(size_t)row * D + c] = (int8_t)quant_i8(__fmul_rn(act[(size_t)row * D + c], inv));
-            if (lane == 0) xscale[row] = __fdiv_rn(sc, 127.0f);
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int j = 0; j < CONV_G; j++) m[j] = max(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
         }
+        unsigned mine = 0u;  // lane j publishes position t + j
+#pragma unroll
+        for (int j = 0; j < CONV_G; j++) mine = (lane == j) ? m[j] : mine;
+        if (lane < CONV_G && t + lane < tend) atomicMax(amax + row0 + t + lane, mine);
     }
 }
 
@@ -64,65 +86,127 @@ conv_act_quant_kernel(const float* __restrict__ xz, int ldx, const float* __rest
 // fused selective scan
 // ---------------------------------------------------------------------------
 constexpr int NS = 16;
-constexpr int SCAN_THREADS = 128;
-constexpr int TC = 32;  // time steps of B/C staged per chunk
+constexpr int SCAN_THREADS = 32;  // one warp per CTA: 32 channels of one sequence
+constexpr int SC = 8;             // time steps per staged chunk
+constexpr int SSTAGES = 2;        // chunks in flight (double buffer)
 
+// Per-warp staging of one chunk: the four per-step inputs of the warp's 32
+// channels (act, decay_mod, z) and the step's B|C row, 4 KB.
+struct ScanStage {
+    float act[SC][32];
+    float mod[SC][32];
+    float z[SC][32];
+    float bc[SC][2 * NS];
+};
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(pred ? 16 : 0)
+                 : "memory");
+}
+
+// Issue the cp.async copies of chunk [t0, t0+SC) into `st` (8 x 16 B per lane).
+__device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __restrict__ act,
+                                                const float* __restrict__ modraw, const float* __restrict__ z,
+                                                const float* __restrict__ bc, int ldbc, int ldz, size_t row0,
+                                                int t0, int L, int d0, int D) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int h2 = 0; h2 < SC * 8 / 32; h2++) {
+        const int idx = lane + 32 * h2;  // 16-byte chunk: step r, quarter q
+        const int r = idx >> 3, q = idx & 7;
+        const int t = t0 + r;
+        const bool okt = t < L;
+        const bool ok = okt && (d0 + 4 * q < D);
+        const size_t row = row0 + (okt ? t : 0);
+        const int c = d0 + (ok ? 4 * q : 0);
+        cp_async16(&st.act[r][4 * q], act + row * D + c, ok);
+        cp_async16(&st.mod[r][4 * q], modraw + row * D + c, ok);
+        cp_async16(&st.z[r][4 * q], z + row * ldz + c, ok);
+        cp_async16(&st.bc[r][4 * q], bc + row * ldbc + (okt ? 4 * q : 0), okt);
+    }
+}
+
+// One warp owns 32 channels of one sequence; each lane carries its channel's
+// 16 fp32 states in registers for the whole sequence.  Inputs arrive through
+// a per-warp double-buffered cp.async ring of SC-step chunks (no block-level
+// barriers).  Each chunk is processed in three phases so that only the state
+// recurrence is serial: (A) decay clamp / dt / x*dt for SC steps, (B) the
+// 16-state convex update and h.C per step, (C) gates, stores and the row
+// absmax reductions for SC steps at once.
 __global__ void __launch_bounds__(SCAN_THREADS)
 ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc,
                 const float* __restrict__ modraw, const float* __restrict__ z, int ldz,
                 const float* __restrict__ base, float* __restrict__ y, float* __restrict__ amax, int L, int D) {
-    __shared__ float sbc[TC][2 * NS];
+    __shared__ __align__(16) ScanStage stage[SSTAGES];
+    const int lane = threadIdx.x;
     const int b = blockIdx.y;
-    const int d = blockIdx.x * SCAN_THREADS + threadIdx.x;
+    const int d0 = blockIdx.x * 32;
+    const int d = d0 + lane;
     const bool active = d < D;
     const int dd = active ? d : 0;
+    const size_t row0 = (size_t)b * L;
 
     float bn[NS], h[NS];
     float bmin = __int_as_float(0x7f800000), bmax = -__int_as_float(0x7f800000);
+    bool bnan = false;
 #pragma unroll
     for (int n = 0; n < NS; n++) {
         bn[n] = base[(size_t)dd * NS + n];
         h[n] = 0.0f;
         bmin = fminf(bmin, bn[n]);
         bmax = fmaxf(bmax, bn[n]);
+        bnan |= (bn[n] != bn[n]);
     }
-    bool bnan = false;
-#pragma unroll
-    for (int n = 0; n < NS; n++) bnan |= (bn[n] != bn[n]);
 
-    const size_t row0 = (size_t)b * L;
-    for (int t0 = 0; t0 < L; t0 += TC) {
-        const int tn = min(TC, L - t0);
-        __syncthreads();
-        for (int i = threadIdx.x; i < tn * 2 * NS; i += SCAN_THREADS) {
-            const int r = i / (2 * NS), q = i % (2 * NS);
-            sbc[r][q] = bc[(row0 + t0 + r) * ldbc + q];
-        }
-        __syncthreads();
-        if (!active) continue;
-        for (int r = 0; r < tn; r++) {
-            const size_t row = row0 + t0 + r;
-            const float xa = act[row * D + d];
-            const float mr = modraw[row * D + d];
-            const float zz = z[row * ldz + d];
-            // decay_mod = ste_clamp(dt_proj(dt), -20, 20)           (:419-422)
-            const float mod = ste_clamp(mr, -20.0f, 20.0f);
-            // dt_val = ste_clamp(squareplus(decay_mod) * 0.01, 1e-3, 0.1)  (:427)
+    const int nchunks = cdiv(L, SC);
+    scan_stage_load(stage[0], act, modraw, z, bc, ldbc, ldz, row0, 0, L, d0, D);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    for (int c = 0; c < nchunks; c++) {
+        ScanStage& st = stage[c & 1];
+        if (c + 1 < nchunks)
+            scan_stage_load(stage[(c + 1) & 1], act, modraw, z, bc, ldbc, ldz, row0, (c + 1) * SC, L, d0, D);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        __syncwarp();
+        const int t0 = c * SC;
+        const int tn = min(SC, L - t0);
+
+        // (A) per (step, channel): decay_mod, dt_val, x*dt   (:419-428)
+        unsigned fast_mask = 0;
+#pragma unroll
+        for (int j = 0; j < SC; j++) {
+            const float mod = ste_clamp(st.mod[j][lane], -20.0f, 20.0f);
             const float dtv = ste_clamp(__fmul_rn(squareplus(mod), 0.01f), 0.001f, 0.1f);
-            // u = (x * dt_val) * B                                   (:428)
-            const float xdt = __fmul_rn(xa, dtv);
-            // decay_nums = ste_clamp(base + decay_mod, 0, 32000)    (:424).  When every
-            // base + mod of this channel is strictly inside (0, 32000) the clamp is the
-            // identity (rounding is monotone, so checking the extremes suffices).
+            st.mod[j][lane] = mod;
+            st.act[j][lane] = __fmul_rn(st.act[j][lane], dtv);  // x * dt_val
+            // decay_nums = ste_clamp(base + mod, 0, 32000) is the identity when every
+            // base + mod of the channel is inside (0, 32000]; rounding is monotone, so
+            // the extremes decide
             const bool inside = !bnan && (__fadd_rn(bmin, mod) > 0.0f) && (__fadd_rn(bmax, mod) <= 32000.0f);
-            float yacc = 0.0f;
-            if (inside) {
+            if (__all_sync(0xffffffffu, inside)) fast_mask |= 1u << j;
+        }
+        // (B) the recurrence, one step at a time
+#pragma unroll 1
+        for (int j = 0; j < tn; j++) {
+            const float mod = st.mod[j][lane];
+            const float xdt = st.act[j][lane];
+            const float4* B4 = reinterpret_cast<const float4*>(&st.bc[j][0]);
+            const float4* C4 = reinterpret_cast<const float4*>(&st.bc[j][NS]);
+            float Bv[NS], Cv[NS];
+#pragma unroll
+            for (int k = 0; k < NS / 4; k++) {
+                const float4 bq = B4[k], cq = C4[k];
+                Bv[4 * k] = bq.x; Bv[4 * k + 1] = bq.y; Bv[4 * k + 2] = bq.z; Bv[4 * k + 3] = bq.w;
+                Cv[4 * k] = cq.x; Cv[4 * k + 1] = cq.y; Cv[4 * k + 2] = cq.z; Cv[4 * k + 3] = cq.w;
+            }
+            if (fast_mask & (1u << j)) {
 #pragma unroll
                 for (int n = 0; n < NS; n++) {
                     const float num = __fadd_rn(bn[n], mod);
-                    const float dec = __fmul_rn(num, 3.0517578125e-05f);  // num / 2^15, exact
-                    const float u = __fmul_rn(xdt, sbc[r][n]);
-                    // h = h * decay + (1 - decay) * u             (:309)
+                    const float dec = __fmul_rn(num, 3.0517578125e-05f);  // num / 2^15 (exact scaling)
+                    const float u = __fmul_rn(xdt, Bv[n]);
+                    // h = h * decay + (1 - decay) * u                   (:309)
                     h[n] = __fadd_rn(__fmul_rn(h[n], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
                 }
             } else {
@@ -130,21 +214,39 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
                 for (int n = 0; n < NS; n++) {
                     const float num = ste_clamp(__fadd_rn(bn[n], mod), 0.0f, 32000.0f);
                     const float dec = __fmul_rn(num, 3.0517578125e-05f);
-                    const float u = __fmul_rn(xdt, sbc[r][n]);
+                    const float u = __fmul_rn(xdt, Bv[n]);
                     h[n] = __fadd_rn(__fmul_rn(h[n], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
                 }
             }
-            // y = matmul(h, C[..., None]): FMA over n = 0..15 from 0    (:440)
+            // y = matmul(h, C[..., None]): fused multiply-add over n = 0..15 from 0   (:440)
+            float yacc = 0.0f;
 #pragma unroll
-            for (int n = 0; n < NS; n++) yacc = __fmaf_rn(h[n], sbc[r][NS + n], yacc);
-            const float out = sigmoid_gate(yacc, zz);
-            y[row * D + d] = out;
-            if (amax) {
-                // non-negative floats order like their bit patterns; NaN bits sort above inf
-                atomicMax(reinterpret_cast<unsigned int*>(amax) + row, __float_as_uint(fabsf(out)));
-            }
+            for (int n = 0; n < NS; n++) yacc = __fmaf_rn(h[n], Cv[n], yacc);
+            st.mod[j][lane] = yacc;  // decay_mod of step j is no longer needed
         }
+        // (C) gate, store, row absmax                                 (:441-444)
+        unsigned m[SC];
+#pragma unroll
+        for (int j = 0; j < SC; j++) {
+            const float out = sigmoid_gate(st.mod[j][lane], st.z[j][lane]);
+            if (j < tn && active) y[(row0 + t0 + j) * D + d] = out;
+            m[j] = (j < tn && active) ? __float_as_uint(fabsf(out)) : 0u;
+        }
+        if (amax) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                for (int j = 0; j < SC; j++) m[j] = max(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
+            }
+            // fp32 bits of non-negative values order like unsigned ints (NaN above +inf)
+            unsigned mine = 0u;  // lane j publishes step j
+#pragma unroll
+            for (int j = 0; j < SC; j++) mine = (lane == j) ? m[j] : mine;
+            if (lane < tn) atomicMax(reinterpret_cast<unsigned int*>(amax) + row0 + t0 + lane, mine);
+        }
+        __syncwarp();  // the buffer is refilled by the next iteration's copies
     }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -189,17 +291,21 @@ static int ew_blocks(int64_t n) {
 }  // namespace mi
 
 extern "C" int mi_conv_act_quant(const float* xz, int ldx, const float* w, const float* bias, float* act, int8_t* xq,
-                                 float* xscale, int batch, int L, int D, void* stream) {
+                                 float* xscale, float* amax_ws, int batch, int L, int D, void* stream) {
     if (!xz || !w || !bias || !act) return MI_ERR_INVALID;
     if ((xq == nullptr) != (xscale == nullptr)) return MI_ERR_INVALID;
+    if (xq && !amax_ws) return MI_ERR_INVALID;
     if (batch <= 0 || L <= 0 || D <= 0 || ldx < D) return MI_ERR_INVALID;
     if (((uintptr_t)w) & 15) return MI_ERR_INVALID;
+    if (batch > 65535 || mi::cdiv(L, mi::ssm::CONV_TC) > 65535) return MI_ERR_UNSUPPORTED;
+    cudaStream_t s = (cudaStream_t)stream;
     const int T = batch * L;
-    int blocks = mi::cdiv(T, 8);
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    mi::ssm::conv_act_quant_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale, L, D,
-                                                                             T);
+    if (amax_ws && cudaMemsetAsync(amax_ws, 0, sizeof(float) * (size_t)T, s) != cudaSuccess) return MI_ERR_CUDA;
+    dim3 grid(mi::cdiv(D, mi::ssm::CONV_THREADS), batch, mi::cdiv(L, mi::ssm::CONV_TC));
+    mi::ssm::conv_act_kernel<<<grid, mi::ssm::CONV_THREADS, 0, s>>>(
+        xz, ldx, w, bias, act, reinterpret_cast<unsigned int*>(amax_ws), L, D);
     MI_CHECK_LAUNCH();
+    if (xq) return mi_quantize_rows(act, D, T, D, xq, D, xscale, amax_ws, stream);
     return MI_OK;
 }
 
@@ -209,6 +315,9 @@ extern "C" int mi_ssm_scan(const float* act, const float* bc, int ldbc, const fl
     if (N != mi::ssm::NS) return MI_ERR_UNSUPPORTED;
     if (batch <= 0 || L <= 0 || D <= 0 || ldbc < 2 * N || ldz < D) return MI_ERR_INVALID;
     if (batch > 65535) return MI_ERR_UNSUPPORTED;
+    // 16-byte asynchronous staging of rows
+    if (((uintptr_t)act | (uintptr_t)bc | (uintptr_t)modraw | (uintptr_t)z) & 15) return MI_ERR_UNSUPPORTED;
+    if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
     dim3 grid(mi::cdiv(D, mi::ssm::SCAN_THREADS), batch);
     mi::ssm::ssm_scan_kernel<<<grid, mi::ssm::SCAN_THREADS, 0, (cudaStream_t)stream>>>(act, bc, ldbc, modraw, z, ldz,
                                                                                        base, y, amax, L, D);

@@ -44,6 +44,7 @@ class _Workspace:
         self.mod = torch.empty(T, di, dtype=f32, device=dev)
         self.y = torch.empty(T, di, dtype=f32, device=dev)
         self.out = torch.empty(T, d, dtype=f32, device=dev)
+        self.amax = torch.empty(T, dtype=f32, device=dev)
 
 
 def _layer_params(blk, dev):
@@ -86,7 +87,7 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
     """Everything between the in_proj output (ws.xz) and the out_proj output (ws.out)."""
     with timer("conv_act_quant"):
         kernels.conv_act_quant(ws.xz, p["conv_w"], p["conv_b"], batch, L, di, act=ws.act, xq=ws.xq_i,
-                               xscale=ws.xs_i)
+                               xscale=ws.xs_i, amax_ws=ws.amax)
     with timer("gemm_x_proj"):
         kernels.bitlinear_i8(ws.xq_i, p["w_x"][0], ws.xs_i, p["w_x"][1], out=ws.xp)
     with timer("quant_dt"):
@@ -94,9 +95,10 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
     with timer("gemm_dt_proj"):
         kernels.bitlinear_i8(ws.dtq, p["w_dt"][0], ws.dts, p["w_dt"][1], out=ws.mod, K=_pad16(R))
     with timer("ssm_scan"):
-        kernels.ssm_scan(ws.act, ws.xp[:, R:], ws.mod, ws.xz[:, di:], p["base"], batch, L, y=ws.y)
+        ws.amax.zero_()
+        kernels.ssm_scan(ws.act, ws.xp[:, R:], ws.mod, ws.xz[:, di:], p["base"], batch, L, y=ws.y, amax=ws.amax)
     with timer("quant_y"):
-        kernels.quantize_rows(ws.y, out=ws.xq_i, xscale=ws.xs_i)
+        kernels.quantize_rows(ws.y, out=ws.xq_i, xscale=ws.xs_i, amax=ws.amax)
     with timer("gemm_out_proj"):
         kernels.bitlinear_i8(ws.xq_i, p["w_out"][0], ws.xs_i, p["w_out"][1], out=ws.out)
 

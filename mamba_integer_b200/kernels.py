@@ -90,7 +90,8 @@ def bitshift_norm(x: torch.Tensor, gamma: torch.Tensor, step, center_once: bool 
 
 
 def quantize_rows(x: torch.Tensor, K: Optional[int] = None, out: Optional[torch.Tensor] = None,
-                  xscale: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+                  xscale: Optional[torch.Tensor] = None, amax: Optional[torch.Tensor] = None
+                  ) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row absmax int8 quantisation of the first K columns of a 2-D fp32
     tensor (row stride taken from x); returns (xq int8 [T, ldq], x_scale [T])."""
     if x.dim() != 2 or x.stride(1) != 1:
@@ -103,7 +104,7 @@ def quantize_rows(x: torch.Tensor, K: Optional[int] = None, out: Optional[torch.
     if xscale is None:
         xscale = torch.empty(T, dtype=torch.float32, device=x.device)
     _lib.check(_lib.load().mi_quantize_rows(x.data_ptr(), x.stride(0), T, K, out.data_ptr(), out.stride(0),
-                                            xscale.data_ptr(), _stream()), "mi_quantize_rows")
+                                            xscale.data_ptr(), _ptr(amax), _stream()), "mi_quantize_rows")
     return out, xscale
 
 
@@ -154,7 +155,7 @@ def bitlinear_i8(A: torch.Tensor, W: torch.Tensor, a_scale: Optional[torch.Tenso
 # conv / scan / element-wise
 # ---------------------------------------------------------------------------
 def conv_act_quant(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, batch: int, L: int, D: int,
-                   act=None, xq=None, xscale=None, quantize: bool = True):
+                   act=None, xq=None, xscale=None, quantize: bool = True, amax_ws=None):
     """Causal depthwise conv + ste_clamp + squareplus (+ int8 quantisation) of
     the first D columns of xz [batch*L, ldx]."""
     T = batch * L
@@ -165,10 +166,13 @@ def conv_act_quant(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, batch:
             xq = torch.empty(T, D, dtype=torch.int8, device=xz.device)
         if xscale is None:
             xscale = torch.empty(T, dtype=torch.float32, device=xz.device)
+        if amax_ws is None:
+            amax_ws = torch.empty(T, dtype=torch.float32, device=xz.device)
     wc = w.detach().to(torch.float32).reshape(D, 4).contiguous()
     bc = bias.detach().to(torch.float32).contiguous()
     _lib.check(_lib.load().mi_conv_act_quant(xz.data_ptr(), xz.stride(0), wc.data_ptr(), bc.data_ptr(),
-                                             act.data_ptr(), _ptr(xq), _ptr(xscale), batch, L, D, _stream()),
+                                             act.data_ptr(), _ptr(xq), _ptr(xscale), _ptr(amax_ws), batch, L, D,
+                                             _stream()),
                "mi_conv_act_quant")
     return act, xq, xscale
 

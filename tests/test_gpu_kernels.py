@@ -209,8 +209,10 @@ def test_ssm_scan_matches_oracle(cuda_dev, bsz, L, D, R):
                     np.ascontiguousarray(z[:, D:].numpy()), base.numpy(), bsz, L)
     dv = lambda t: t.to(cuda_dev)  # noqa: E731
     xpd, zd = dv(xp), dv(z)
-    y = k.ssm_scan(dv(act), xpd[:, R:], dv(modraw), zd[:, D:], dv(base), bsz, L)
+    amax = torch.zeros(T, device=cuda_dev)
+    y = k.ssm_scan(dv(act), xpd[:, R:], dv(modraw), zd[:, D:], dv(base), bsz, L, amax=amax)
     _eq(y, y_ref, "ssm y")
+    _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
 
 
 def test_scan_convex_and_elementwise_match_reference_fixtures(cuda_dev):
