@@ -142,6 +142,73 @@ class EventTimer:
         return {k: [a.elapsed_time(b) for a, b in v] for k, v in self.ev.items()}
 
 
+def _time_launches(fn, iters: int, flush: torch.Tensor | None):
+    """Average device time of fn() over iters launches (CUDA events on the
+    current stream); the L2 flush between launches is outside the events."""
+    tot = 0.0
+    for _ in range(iters):
+        if flush is not None:
+            flush.add_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    return tot / iters
+
+
+def secondary_metrics(dev, warmup: int = 3, iters: int = 5):
+    """The other two BASELINE metrics on their own configs: the integer scan
+    (config 2, GB/s) and the BitLinear GEMM (config 3, int8 TOP/s)."""
+    from mamba_integer_b200 import _lib, kernels, synth
+
+    hbm, bf16, src = peaks()
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
+    out = {}
+    # config 2: x [8,4096,2048], B/C [8,4096,16], n [2048,16] int32, y int32, h int32
+    x, B, C, n = (t.to(dev) for t in synth.scan_i32_inputs())
+    bsz, L, D = x.shape
+    h = torch.zeros(bsz, D, 16, dtype=torch.int32, device=dev)
+    y = torch.empty(bsz, L, D, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+
+    def run_scan():
+        h.zero_()
+        _lib.check(lib.mi_scan_i32(x.data_ptr(), B.data_ptr(), C.data_ptr(), n.data_ptr(), 15, y.data_ptr(), None,
+                                   h.data_ptr(), bsz, L, D, 16, st), "mi_scan_i32")
+
+    for _ in range(warmup):
+        run_scan()
+    ms = _time_launches(run_scan, iters, None)  # inputs (268 MB) larger than L2
+    err = _lib.device_error(st)
+    nbytes = 542244864
+    out["scan_i32"] = {"config": "config2: batch 8, L 4096, d_inner 2048, d_state 16, int32 y and h",
+                       "ms": ms, "GB_per_s": nbytes / ms / 1e6, "hbm_frac": nbytes / ms / 1e6 / hbm,
+                       "G_state_updates_per_s": bsz * L * D * 16 / ms / 1e6, "device_error_word": err,
+                       "bytes_per_call": nbytes, "peak_source": src}
+    del x, B, C, n, h, y
+    # config 3: A int8 [16384, 2048] x W ternary int8 [8192, 2048] -> int32 C
+    A, a_scale, Wq, ws = synth.bitlinear_inputs()
+    A, Wq = A.to(dev), Wq.to(dev)
+    Cm = torch.empty(A.shape[0], Wq.shape[0], dtype=torch.int32, device=dev)
+
+    def run_gemm():
+        kernels.bitlinear_i8(A, Wq, out=Cm)
+
+    for _ in range(warmup):
+        run_gemm()
+    ms = _time_launches(run_gemm, iters, flush)  # A and W fit in L2: flush between launches
+    ops = 2.0 * A.shape[0] * Wq.shape[0] * A.shape[1]
+    tops = ops / ms / 1e9
+    out["bitlinear_i8"] = {"config": "config3: M 16384, K 2048, N 8192, int32 out", "ms": ms, "TOP_per_s": tops,
+                           "int8_peak_frac": tops / (2.0 * bf16),
+                           "int8_peak": 2.0 * bf16, "peak_note": "2 x measured dense bf16 (nominal int8:bf16 = 2)",
+                           "output_GB_per_s": Cm.numel() * 4 / ms / 1e6}
+    return out
+
+
 def cpu_baseline(n_tokens: int = 256, threads: int = 0):
     """The CPU restatement of the reference path (full 24 layers + lm_head) on
     one sequence of n_tokens of the config-4 workload."""
@@ -196,6 +263,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the config-2 scan / config-3 GEMM lines")
     # smaller shapes for profiling captures only (the reported workload is 64 x 2048)
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     ap.add_argument("--seq", type=int, default=SEQ_LEN)
@@ -295,6 +363,11 @@ def main():
         tim = EventTimer()
         eng.forward(ids_dev, logits=logits, timer=tim)
         per_k = tim.per_kernel()
+        secondary = None
+        if rank == 0 and not args.no_secondary:
+            del logits
+            torch.cuda.empty_cache()
+            secondary = secondary_metrics(dev)
 
     hbm, bf16, src = peaks()
     totals = {k: sum(v) for k, v in per_k.items()}
@@ -340,6 +413,7 @@ def main():
             "kernel_breakdown": breakdown,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

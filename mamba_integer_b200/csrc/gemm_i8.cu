@@ -42,7 +42,8 @@ struct Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
     static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per accumulator
     static constexpr int EPI_BOXES = (BN + 31) / 32;   // 32-column output boxes per tile
-    static constexpr int STG_BYTES = EPI_WARPS * 2 * 4096;  // two staging boxes per epilogue warp
+    static constexpr int STG_BUFS = 4;                              // staging boxes per epilogue warp
+    static constexpr int STG_BYTES = EPI_WARPS * STG_BUFS * 4096;  // (bulk stores kept in flight)
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the 128B swizzle");
@@ -259,11 +260,11 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // ---------------- epilogue (warps 2..5) ----------------
         // A warp may only touch the TMEM lane quarter warp % 4: it owns the tile
         // rows q*32 .. q*32+31.  Each 32-column slab is dequantised, written in
-        // the 128-byte-swizzled layout of a 32x32 TMA box into one of two
+        // the 128-byte-swizzled layout of a 32x32 TMA box into one of STG_BUFS
         // staging buffers, and stored with a bulk tensor copy (TMA clips rows
-        // >= M and columns >= N).
+        // >= M and columns >= N); up to STG_BUFS stores stay in flight per warp.
         const int q = warp & 3;
-        const uint32_t stg = stg_base + (uint32_t)((warp - 2) * 2 * 4096);
+        const uint32_t stg = stg_base + (uint32_t)((warp - 2) * C::STG_BUFS * 4096);
         unsigned char* stg_g = gbase + (stg - base);
         const float ws = (epi == MI_EPI_F32_SCALED) ? *w_scale : 0.0f;
         const float os = out_scale ? *out_scale : 1.0f;
@@ -299,10 +300,11 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                         r[j] = __float_as_uint(v);
                     }
                 }
-                // the staging buffer used two stores ago must have been read
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+                // the staging buffer used STG_BUFS stores ago must have been read
+                static_assert(C::STG_BUFS == 4, "wait_group.read count below");
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 3;\n" ::: "memory");
                 __syncwarp();
-                unsigned char* rowp = stg_g + (nst & 1) * 4096 + lane * 128;
+                unsigned char* rowp = stg_g + (nst & (C::STG_BUFS - 1)) * 4096 + lane * 128;
 #pragma unroll
                 for (int c = 0; c < 8; c++) {
                     const int phys = c ^ (lane & 7);
@@ -313,7 +315,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 __syncwarp();
                 if (lane == 0) {
                     const int x = n0 + cb * 32, y = m0 + q * 32;
-                    if (x < N && y < M) tma_store_2d(&tmC, stg + (nst & 1) * 4096, x, y);
+                    if (x < N && y < M) tma_store_2d(&tmC, stg + (nst & (C::STG_BUFS - 1)) * 4096, x, y);
                     asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
                 }
             }

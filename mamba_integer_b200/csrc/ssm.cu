@@ -97,7 +97,10 @@ struct ScanStage {
     float mod[SC][32];
     float z[SC][32];
     float bc[SC][2 * NS];
+    int32_t dtq[SC][16];  // fused dt_proj: int8 dt row (up to 64 values) as words
+    float dts[SC];        // fused dt_proj: per-row activation scale
 };
+constexpr int MAX_RW = 16;  // dt_rank padded to 16 values <= 64
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
     const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
@@ -105,11 +108,28 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pr
                  : "memory");
 }
 
-// Issue the cp.async copies of chunk [t0, t0+SC) into `st` (8 x 16 B per lane).
-__device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __restrict__ act,
-                                                const float* __restrict__ modraw, const float* __restrict__ z,
-                                                const float* __restrict__ bc, int ldbc, int ldz, size_t row0,
-                                                int t0, int L, int d0, int D) {
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pred) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(sa), "l"(gmem), "r"(pred ? 4 : 0)
+                 : "memory");
+}
+
+// Inputs of the decay modulation: either the dt_proj output (RW == 0) or the
+// quantised dt rows + scales and the dt_proj weights (RW = words per row).
+struct DtSource {
+    const float* modraw;   // [T, D] (RW == 0)
+    const int8_t* dtq;     // [T, ldq] int8 (RW > 0)
+    int ldq;
+    const float* dts;      // [T]
+    const int8_t* w;       // [D, 4*RW] int8 ternary dt_proj weights
+    const float* w_scale;  // [1]
+};
+
+// Issue the cp.async copies of chunk [t0, t0+SC) into `st` (16-byte copies).
+template <int RW>
+__device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __restrict__ act, const DtSource& src,
+                                                const float* __restrict__ z, const float* __restrict__ bc, int ldbc,
+                                                int ldz, size_t row0, int t0, int L, int d0, int D) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int h2 = 0; h2 < SC * 8 / 32; h2++) {
@@ -121,9 +141,23 @@ __device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __re
         const size_t row = row0 + (okt ? t : 0);
         const int c = d0 + (ok ? 4 * q : 0);
         cp_async16(&st.act[r][4 * q], act + row * D + c, ok);
-        cp_async16(&st.mod[r][4 * q], modraw + row * D + c, ok);
+        if (RW == 0) cp_async16(&st.mod[r][4 * q], src.modraw + row * D + c, ok);
         cp_async16(&st.z[r][4 * q], z + row * ldz + c, ok);
         cp_async16(&st.bc[r][4 * q], bc + row * ldbc + (okt ? 4 * q : 0), okt);
+    }
+    if (RW > 0) {
+        // dt rows: SC rows x (RW/4) chunks of 16 bytes; scales: SC x 4 bytes
+        for (int idx = lane; idx < SC * (RW / 4); idx += 32) {
+            const int r = idx / (RW / 4), q = idx % (RW / 4);
+            const int t = t0 + r;
+            const bool okt = t < L;
+            const size_t row = row0 + (okt ? t : 0);
+            cp_async16(&st.dtq[r][4 * q], src.dtq + row * src.ldq + 16 * q, okt);
+        }
+        if (lane < SC) {
+            const int t = t0 + lane;
+            cp_async4(&st.dts[lane], src.dts + row0 + (t < L ? t : 0), t < L);
+        }
     }
 }
 
@@ -134,10 +168,19 @@ __device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __re
 // recurrence is serial: (A) decay clamp / dt / x*dt for SC steps, (B) the
 // 16-state convex update and h.C per step, (C) gates, stores and the row
 // absmax reductions for SC steps at once.
-__global__ void __launch_bounds__(SCAN_THREADS)
-ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc,
-                const float* __restrict__ modraw, const float* __restrict__ z, int ldz,
-                const float* __restrict__ base, float* __restrict__ y, float* __restrict__ amax, int L, int D) {
+//
+// RW > 0 fuses the dt_proj BitLinear: each lane keeps its channel's ternary
+// dt_proj weights (4*RW int8) in registers and forms the exact int32 dot
+// product with the step's quantised dt row by dp4a, then applies the
+// BitLinear rescale acc * (w_scale * dt_scale[t]) exactly as the GEMM
+// epilogue does (src/rational_bitnet.py:204-208).
+// (22 one-warp CTAs per SM by registers and shared memory: all 3072 CTAs of a
+// 64-sequence x 1536-channel layer are resident at once.)
+template <int RW>
+__global__ void __launch_bounds__(SCAN_THREADS, 22)
+ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
+                const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
+                float* __restrict__ amax, int L, int D) {
     __shared__ __align__(16) ScanStage stage[SSTAGES];
     const int lane = threadIdx.x;
     const int b = blockIdx.y;
@@ -147,30 +190,62 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
     const int dd = active ? d : 0;
     const size_t row0 = (size_t)b * L;
 
-    float bn[NS], h[NS];
+    int32_t wd[RW > 0 ? RW : 1];
+    float wsc = 0.0f;
+    if (RW > 0) {
+        const int4* wrow = reinterpret_cast<const int4*>(src.w + (size_t)dd * (4 * RW));
+#pragma unroll
+        for (int k = 0; k < RW / 4; k++) {
+            const int4 v = wrow[k];
+            wd[4 * k] = v.x; wd[4 * k + 1] = v.y; wd[4 * k + 2] = v.z; wd[4 * k + 3] = v.w;
+        }
+        wsc = *src.w_scale;
+    }
+
+    // states and base / 2^15 in pairs for the packed f32x2 arithmetic
+    float2 h2[NS / 2], bs2[NS / 2];
     float bmin = __int_as_float(0x7f800000), bmax = -__int_as_float(0x7f800000);
     bool bnan = false;
 #pragma unroll
-    for (int n = 0; n < NS; n++) {
-        bn[n] = base[(size_t)dd * NS + n];
-        h[n] = 0.0f;
-        bmin = fminf(bmin, bn[n]);
-        bmax = fmaxf(bmax, bn[n]);
-        bnan |= (bn[n] != bn[n]);
+    for (int i = 0; i < NS / 2; i++) {
+        const float b0 = base[(size_t)dd * NS + 2 * i], b1 = base[(size_t)dd * NS + 2 * i + 1];
+        bs2[i] = make_float2(__fmul_rn(b0, 3.0517578125e-05f), __fmul_rn(b1, 3.0517578125e-05f));
+        h2[i] = make_float2(0.0f, 0.0f);
+        bmin = fminf(bmin, fminf(b0, b1));
+        bmax = fmaxf(bmax, fmaxf(b0, b1));
+        bnan |= (b0 != b0) | (b1 != b1);
     }
 
     const int nchunks = cdiv(L, SC);
-    scan_stage_load(stage[0], act, modraw, z, bc, ldbc, ldz, row0, 0, L, d0, D);
+    scan_stage_load<RW>(stage[0], act, src, z, bc, ldbc, ldz, row0, 0, L, d0, D);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     for (int c = 0; c < nchunks; c++) {
         ScanStage& st = stage[c & 1];
         if (c + 1 < nchunks)
-            scan_stage_load(stage[(c + 1) & 1], act, modraw, z, bc, ldbc, ldz, row0, (c + 1) * SC, L, d0, D);
+            scan_stage_load<RW>(stage[(c + 1) & 1], act, src, z, bc, ldbc, ldz, row0, (c + 1) * SC, L, d0, D);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
         __syncwarp();
         const int t0 = c * SC;
         const int tn = min(SC, L - t0);
+        if (RW > 0) {
+            // decay_mod before its clamp = dt_proj(dt): exact int32 dot product of the
+            // int8 dt row with the ternary weights, then acc * (w_scale * dt_scale)
+#pragma unroll
+            for (int j = 0; j < SC; j++) {
+                const int4* q4 = reinterpret_cast<const int4*>(&st.dtq[j][0]);
+                int acc = 0;
+#pragma unroll
+                for (int k = 0; k < RW / 4; k++) {
+                    const int4 qv = q4[k];
+                    acc = __dp4a(qv.x, wd[4 * k], acc);
+                    acc = __dp4a(qv.y, wd[4 * k + 1], acc);
+                    acc = __dp4a(qv.z, wd[4 * k + 2], acc);
+                    acc = __dp4a(qv.w, wd[4 * k + 3], acc);
+                }
+                st.mod[j][lane] = __fmul_rn((float)acc, __fmul_rn(wsc, st.dts[j]));
+            }
+        }
 
         // (A) per (step, channel): decay_mod, dt_val, x*dt   (:419-428)
         unsigned fast_mask = 0;
@@ -180,10 +255,15 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
             const float dtv = ste_clamp(__fmul_rn(squareplus(mod), 0.01f), 0.001f, 0.1f);
             st.mod[j][lane] = mod;
             st.act[j][lane] = __fmul_rn(st.act[j][lane], dtv);  // x * dt_val
-            // decay_nums = ste_clamp(base + mod, 0, 32000) is the identity when every
-            // base + mod of the channel is inside (0, 32000]; rounding is monotone, so
-            // the extremes decide
-            const bool inside = !bnan && (__fadd_rn(bmin, mod) > 0.0f) && (__fadd_rn(bmax, mod) <= 32000.0f);
+            // decay_nums = ste_clamp(v, 0, 32000), v = base + mod, equals the plain
+            // clamp(v, 0, 32000) whenever v <= 64000: for v > 32000 the difference
+            // 32000 - v is exact (Sterbenz) so v + (32000 - v) = 32000, for v < 0 it
+            // gives +0, and inside the range it is the identity.  Rounding is monotone,
+            // so the channel's largest base decides.  base >= 1 and a mod that is 0 or
+            // not tiny keep base/2^15 and mod/2^15 exact (no subnormals), which the
+            // fast path below relies on.
+            const bool inside = !bnan && (bmin >= 1.0f) && (__fadd_rn(bmax, mod) <= 64000.0f) &&
+                                (mod == 0.0f || fabsf(mod) >= 1e-30f);
             if (__all_sync(0xffffffffu, inside)) fast_mask |= 1u << j;
         }
         // (B) the recurrence, one step at a time
@@ -191,37 +271,53 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
         for (int j = 0; j < tn; j++) {
             const float mod = st.mod[j][lane];
             const float xdt = st.act[j][lane];
-            const float4* B4 = reinterpret_cast<const float4*>(&st.bc[j][0]);
-            const float4* C4 = reinterpret_cast<const float4*>(&st.bc[j][NS]);
-            float Bv[NS], Cv[NS];
-#pragma unroll
-            for (int k = 0; k < NS / 4; k++) {
-                const float4 bq = B4[k], cq = C4[k];
-                Bv[4 * k] = bq.x; Bv[4 * k + 1] = bq.y; Bv[4 * k + 2] = bq.z; Bv[4 * k + 3] = bq.w;
-                Cv[4 * k] = cq.x; Cv[4 * k + 1] = cq.y; Cv[4 * k + 2] = cq.z; Cv[4 * k + 3] = cq.w;
-            }
+            const float2* B2 = reinterpret_cast<const float2*>(&st.bc[j][0]);
+            const float2* C2 = reinterpret_cast<const float2*>(&st.bc[j][NS]);
             if (fast_mask & (1u << j)) {
+                // decay = clamp(base + mod, 0, 32000) / 2^15
+                //       = clamp(base/2^15 + mod/2^15, 0, 32000/2^15): both scalings are
+                // exact, the sum rounds once, and scaling by 2^-15 commutes with
+                // rounding and with the clamp away from subnormals
+                const float ms = __fmul_rn(mod, 3.0517578125e-05f);
 #pragma unroll
-                for (int n = 0; n < NS; n++) {
-                    const float num = __fadd_rn(bn[n], mod);
-                    const float dec = __fmul_rn(num, 3.0517578125e-05f);  // num / 2^15 (exact scaling)
-                    const float u = __fmul_rn(xdt, Bv[n]);
-                    // h = h * decay + (1 - decay) * u                   (:309)
-                    h[n] = __fadd_rn(__fmul_rn(h[n], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                for (int i = 0; i < NS / 2; i++) {
+                    const float2 bq = B2[i];
+                    float hv[2] = {h2[i].x, h2[i].y};
+                    const float bb[2] = {bs2[i].x, bs2[i].y}, Bq[2] = {bq.x, bq.y};
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const float dec = clamp_t(__fadd_rn(bb[e], ms), 0.0f, 0.9765625f);  // 32000 / 2^15
+                        const float u = __fmul_rn(xdt, Bq[e]);
+                        // h = h * decay + (1 - decay) * u                   (:309)
+                        hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                    }
+                    h2[i] = make_float2(hv[0], hv[1]);
                 }
             } else {
 #pragma unroll
-                for (int n = 0; n < NS; n++) {
-                    const float num = ste_clamp(__fadd_rn(bn[n], mod), 0.0f, 32000.0f);
-                    const float dec = __fmul_rn(num, 3.0517578125e-05f);
-                    const float u = __fmul_rn(xdt, Bv[n]);
-                    h[n] = __fadd_rn(__fmul_rn(h[n], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                for (int i = 0; i < NS / 2; i++) {
+                    const float2 bq = B2[i];
+                    float hv[2] = {h2[i].x, h2[i].y};
+                    const float bb[2] = {bs2[i].x, bs2[i].y}, Bq[2] = {bq.x, bq.y};
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const float bn = __fmul_rn(bb[e], 32768.0f);  // exact: back to base
+                        const float num = ste_clamp(__fadd_rn(bn, mod), 0.0f, 32000.0f);
+                        const float dec = __fmul_rn(num, 3.0517578125e-05f);
+                        const float u = __fmul_rn(xdt, Bq[e]);
+                        hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                    }
+                    h2[i] = make_float2(hv[0], hv[1]);
                 }
             }
             // y = matmul(h, C[..., None]): fused multiply-add over n = 0..15 from 0   (:440)
             float yacc = 0.0f;
 #pragma unroll
-            for (int n = 0; n < NS; n++) yacc = __fmaf_rn(h[n], Cv[n], yacc);
+            for (int i = 0; i < NS / 2; i++) {
+                const float2 cq = C2[i];
+                yacc = __fmaf_rn(h2[i].x, cq.x, yacc);
+                yacc = __fmaf_rn(h2[i].y, cq.y, yacc);
+            }
             st.mod[j][lane] = yacc;  // decay_mod of step j is no longer needed
         }
         // (C) gate, store, row absmax                                 (:441-444)
@@ -319,8 +415,49 @@ extern "C" int mi_ssm_scan(const float* act, const float* bc, int ldbc, const fl
     if (((uintptr_t)act | (uintptr_t)bc | (uintptr_t)modraw | (uintptr_t)z) & 15) return MI_ERR_UNSUPPORTED;
     if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
     dim3 grid(mi::cdiv(D, mi::ssm::SCAN_THREADS), batch);
-    mi::ssm::ssm_scan_kernel<<<grid, mi::ssm::SCAN_THREADS, 0, (cudaStream_t)stream>>>(act, bc, ldbc, modraw, z, ldz,
-                                                                                       base, y, amax, L, D);
+    mi::ssm::DtSource src{modraw, nullptr, 0, nullptr, nullptr, nullptr};
+    mi::ssm::ssm_scan_kernel<0><<<grid, mi::ssm::SCAN_THREADS, 0, (cudaStream_t)stream>>>(act, bc, ldbc, src, z, ldz,
+                                                                                          base, y, amax, L, D);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const int8_t* dtq, int ldq, const float* dts,
+                              const int8_t* w_dt, const float* w_dt_scale, int R, const float* z, int ldz,
+                              const float* base, float* y, float* amax, int batch, int L, int D, int N, void* stream) {
+    if (!act || !bc || !dtq || !dts || !w_dt || !w_dt_scale || !z || !base || !y) return MI_ERR_INVALID;
+    if (N != mi::ssm::NS) return MI_ERR_UNSUPPORTED;
+    if (batch <= 0 || L <= 0 || D <= 0 || R <= 0 || ldbc < 2 * N || ldz < D) return MI_ERR_INVALID;
+    const int R16 = (R + 15) / 16 * 16;
+    if (R16 > 4 * mi::ssm::MAX_RW || ldq < R16 || (ldq & 15)) return MI_ERR_UNSUPPORTED;
+    if (batch > 65535) return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)act | (uintptr_t)bc | (uintptr_t)z | (uintptr_t)dtq | (uintptr_t)w_dt) & 15)
+        return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)dts) & 3) return MI_ERR_UNSUPPORTED;
+    if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
+    dim3 grid(mi::cdiv(D, mi::ssm::SCAN_THREADS), batch);
+    mi::ssm::DtSource src{nullptr, dtq, ldq, dts, w_dt, w_dt_scale};
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (R16 / 4) {
+        case 4:
+            mi::ssm::ssm_scan_kernel<4><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
+                                                                                amax, L, D);
+            break;
+        case 8:
+            mi::ssm::ssm_scan_kernel<8><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
+                                                                                amax, L, D);
+            break;
+        case 12:
+            mi::ssm::ssm_scan_kernel<12><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
+                                                                                 amax, L, D);
+            break;
+        case 16:
+            mi::ssm::ssm_scan_kernel<16><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
+                                                                                 amax, L, D);
+            break;
+        default:
+            return MI_ERR_UNSUPPORTED;
+    }
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

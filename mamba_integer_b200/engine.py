@@ -41,7 +41,6 @@ class _Workspace:
         self.xp = torch.empty(T, R + 2 * N, dtype=f32, device=dev)
         self.dtq = torch.zeros(T, _pad16(R), dtype=i8, device=dev)
         self.dts = torch.empty(T, dtype=f32, device=dev)
-        self.mod = torch.empty(T, di, dtype=f32, device=dev)
         self.y = torch.empty(T, di, dtype=f32, device=dev)
         self.out = torch.empty(T, d, dtype=f32, device=dev)
         self.amax = torch.empty(T, dtype=f32, device=dev)
@@ -92,11 +91,11 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
         kernels.bitlinear_i8(ws.xq_i, p["w_x"][0], ws.xs_i, p["w_x"][1], out=ws.xp)
     with timer("quant_dt"):
         kernels.quantize_rows(ws.xp, K=R, out=ws.dtq, xscale=ws.dts)
-    with timer("gemm_dt_proj"):
-        kernels.bitlinear_i8(ws.dtq, p["w_dt"][0], ws.dts, p["w_dt"][1], out=ws.mod, K=_pad16(R))
     with timer("ssm_scan"):
+        # dt_proj is fused into the scan (each channel's dot product by dp4a)
         ws.amax.zero_()
-        kernels.ssm_scan(ws.act, ws.xp[:, R:], ws.mod, ws.xz[:, di:], p["base"], batch, L, y=ws.y, amax=ws.amax)
+        kernels.ssm_scan_dt(ws.act, ws.xp[:, R:], ws.dtq, ws.dts, p["w_dt"][0], p["w_dt"][1], R, ws.xz[:, di:],
+                            p["base"], batch, L, y=ws.y, amax=ws.amax)
     with timer("quant_y"):
         kernels.quantize_rows(ws.y, out=ws.xq_i, xscale=ws.xs_i, amax=ws.amax)
     with timer("gemm_out_proj"):

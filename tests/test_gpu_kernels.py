@@ -215,6 +215,37 @@ def test_ssm_scan_matches_oracle(cuda_dev, bsz, L, D, R):
     _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
 
 
+@pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (2, 9, 96, 64), (1, 33, 64, 20)])
+def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R):
+    """dt_proj fused into the scan: same result as quantise -> BitLinear -> scan."""
+    k = _mi()
+    g = torch.Generator().manual_seed(5 * bsz + L + D + R)
+    T = bsz * L
+    R16 = (R + 15) // 16 * 16
+    act = torch.rand(T, D, generator=g) * 5
+    xp = torch.randn(T, R + 32, generator=g) * 2
+    z = torch.randn(T, 2 * D, generator=g) * 3
+    base = torch.randint(29492, 32736, (D, 16), generator=g).float()
+    wdt = torch.randint(-1, 2, (D, R), generator=g, dtype=torch.int8)
+    ws = np.float32(2.0 ** -5)
+    dtq, dts = orc.quant_rows(np.ascontiguousarray(xp[:, :R].numpy()))
+    modraw = orc.bitlinear(dtq, dts, wdt.numpy(), ws)
+    y_ref = orc.ssm(act.numpy(), np.ascontiguousarray(xp[:, R:].numpy()), modraw,
+                    np.ascontiguousarray(z[:, D:].numpy()), base.numpy(), bsz, L)
+    dv = lambda t: t.to(cuda_dev)  # noqa: E731
+    dtq_d = torch.zeros(T, R16, dtype=torch.int8, device=cuda_dev)
+    dts_d = torch.empty(T, device=cuda_dev)
+    xpd, zd = dv(xp), dv(z)
+    k.quantize_rows(xpd, K=R, out=dtq_d, xscale=dts_d)
+    w16 = torch.zeros(D, R16, dtype=torch.int8)
+    w16[:, :R] = wdt
+    amax = torch.zeros(T, device=cuda_dev)
+    y = k.ssm_scan_dt(dv(act), xpd[:, R:], dtq_d, dts_d, dv(w16), dv(torch.tensor([ws])), R, zd[:, D:], dv(base),
+                      bsz, L, amax=amax)
+    _eq(y, y_ref, "fused-dt ssm y")
+    _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
+
+
 def test_scan_convex_and_elementwise_match_reference_fixtures(cuda_dev):
     import os
     k = _mi()
