@@ -58,8 +58,8 @@ def algorithmic_work(name: str, T: int, d=768, di=1536, R=48, N=16, V=32768):
         return "tensor", 2.0 * T * d * di
     if name == "gemm_lm_head":
         return "tensor", 2.0 * T * V * d
-    if name == "ssm_scan":  # reads act, decay_mod, z, B|C; writes y
-        return "hbm", T * di * 4 * 4 + T * 2 * N * 4 + di * N * 4
+    if name == "ssm_scan":  # reads act, z, int8 dt row + scale, B|C; writes y (dt_proj fused)
+        return "hbm", T * di * 4 * 3 + T * (R + 4) + T * 2 * N * 4 + di * N * 4 + di * R
     if name == "conv_act_quant":  # reads x half of xz; writes act, xq, scale
         return "hbm", T * di * 4 + T * di * 4 + T * di + T * 4
     if name == "rowprep":  # reads residual + delta; writes residual, xq, scale
@@ -69,6 +69,18 @@ def algorithmic_work(name: str, T: int, d=768, di=1536, R=48, N=16, V=32768):
     if name == "quant_dt":
         return "hbm", T * R * 4 + T * R + T * 4
     return "hbm", 0.0
+
+
+def measured_traffic(kernel: str, T: int):
+    """DRAM bytes (read + write) per launch from the committed ncu summary
+    profiles/roofline_traffic.json (captured at a smaller token count and
+    scaled by tokens; the kernels' traffic is linear in tokens), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            t = json.load(f)[kernel]
+        return t["dram_bytes_per_launch"] * T / t["tokens"]
+    except Exception:
+        return None
 
 
 class ClockSampler:
@@ -267,6 +279,8 @@ def main():
     # smaller shapes for profiling captures only (the reported workload is 64 x 2048)
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     ap.add_argument("--seq", type=int, default=SEQ_LEN)
+    ap.add_argument("--scan-split", type=int, default=0, choices=[0, 1, 2, 4],
+                    help="lanes per channel of the fused scan (0 = automatic)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -296,6 +310,7 @@ def main():
     model.load_state_dict(sd)
     model = model.to(dev).eval()
     eng = model.engine()
+    eng.scan_split = args.scan_split
     gb, sl = args.batch, args.seq
     ids_all = synth.input_ids("c4", gb, sl)
     per = gb // world
@@ -343,7 +358,11 @@ def main():
         # end to end through the public API: pinned host ids -> device, forward,
         # last-position logits -> pinned host
         last_host = torch.empty(b_local, V, dtype=torch.float32).pin_memory()
-        e2e_steps = max(1, min(args.steps, 3))
+        e2e_steps = args.steps
+        # one untimed pass so the logits allocation of the API call is cached
+        out = model(ids_host.to(dev, non_blocking=True))
+        last_host.copy_(out[:, -1, :], non_blocking=True)
+        del out
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -408,7 +427,7 @@ def main():
                     "d2h_bytes_per_step": int(b_local * V * 4)},
             "gpu_launches": launches_per_forward(cfg["n_layer"]) * args.steps,
             "roofline": {"kernel": dom, "bound": bound, "achieved": achieved, "peak": peak, "unit": unit,
-                         "frac": achieved / peak, "traffic": None, "peak_source": src,
+                         "frac": achieved / peak, "traffic": measured_traffic(dom, T_local), "peak_source": src,
                          "avg_launch_ms": avg_ms},
             "kernel_breakdown": breakdown,
             "clocks": clk.summary(),

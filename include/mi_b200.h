@@ -151,13 +151,15 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * w_dt int8 [D, ceil16(R)] (zero-padded) and w_dt_scale [1]; each channel
  * forms the exact int32 dot product and the BitLinear rescale
  * acc * (w_dt_scale * dts[t]) itself.  R <= 64.
+ * split = lanes per channel (1, 2 or 4; 0 = chosen from batch*D vs the SM
+ * count): more lanes per channel keep small per-GPU batches occupied.
  * Replaces: dt_proj + DyadicScanFunction section, src/mamba_integer_model.py:419-444
  * (BitLinear rescale: src/rational_bitnet.py:204-208).
  */
 int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const int8_t* dtq, int ldq,
                    const float* dts, const int8_t* w_dt, const float* w_dt_scale, int R,
                    const float* z, int ldz, const float* base, float* y, float* amax, int batch,
-                   int L, int D, int N, void* stream);
+                   int L, int D, int N, int split, void* stream);
 
 /* Convex dyadic scan on materialised inputs: h = h*(n/2^15) + (1-n/2^15)*u.
  * u, nums, h [batch, L, DN].

@@ -35,7 +35,7 @@ SIGNATURES = {
     "mi_bitlinear_i8": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_ssm_scan": [_p, _p, _i, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
-    "mi_ssm_scan_dt": [_p, _p, _i, _p, _i, _p, _p, _p, _i, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
+    "mi_ssm_scan_dt": [_p, _p, _i, _p, _i, _p, _p, _p, _i, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_scan_convex": [_p, _p, _p, _i, _i, _i, _p],
     "mi_squareplus_clamp": [_p, _p, _i64, _f, _f, _p],
     "mi_ste_clamp": [_p, _p, _i64, _f, _f, _p],

@@ -333,6 +333,241 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------
+// A-resident variant for K <= 768 (in_proj, lm_head): the 128-row block of A
+// (up to 6 K-slices, 96 KB) is loaded once per work unit and kept in shared
+// memory while the unit's N tiles stream their weight slices through a
+// 6-deep ring, so A crosses L2 once per unit instead of once per N tile and
+// the ring holds twice the bytes in flight of the streaming kernel.
+// A unit is (M tile, group of consecutive N tiles); units go round-robin to
+// the persistent CTAs.
+// ---------------------------------------------------------------------------
+constexpr int ARES_MAXK = 6;    // K slices held (K <= 768)
+constexpr int ARES_SB = 6;      // weight ring depth
+constexpr int ARES_BN = 128;
+constexpr int ARES_STG = 2;     // staging boxes per epilogue warp
+constexpr int ARES_A_BYTES = ARES_MAXK * BM * BK;              // 96 KB
+constexpr int ARES_B_BYTES = ARES_BN * BK;                     // 16 KB per slice
+constexpr int ARES_STG_BYTES = EPI_WARPS * ARES_STG * 4096;    // 32 KB
+constexpr int ARES_SMEM = 1024 + ARES_A_BYTES + ARES_SB * ARES_B_BYTES + ARES_STG_BYTES + 256;
+static_assert(ARES_SMEM <= 227 * 1024, "shared memory per CTA");
+
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
+                    const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K,
+                    int epi, int groups) {
+    constexpr int BN = ARES_BN;
+    constexpr int TMEM_COLS = 128;
+    constexpr int EPI_BOXES = BN / 32;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw);
+    const uint32_t a_base = base;                                   // ARES_MAXK x 16 KB
+    const uint32_t b_base = a_base + ARES_A_BYTES;                  // ARES_SB x 16 KB
+    const uint32_t stg_base = b_base + ARES_SB * ARES_B_BYTES;      // staging
+    const uint32_t bars = stg_base + ARES_STG_BYTES;
+    // barriers: bfull[SB], bempty[SB], tfull[2], tempty[2], afull, aempty; then TMEM slot, abort flag
+    auto bfull_bar = [&](int s) { return bars + 8u * s; };
+    auto bempty_bar = [&](int s) { return bars + 8u * (ARES_SB + s); };
+    auto tfull_bar = [&](int a) { return bars + 8u * (2 * ARES_SB + a); };
+    auto tempty_bar = [&](int a) { return bars + 8u * (2 * ARES_SB + 2 + a); };
+    const uint32_t afull_bar = bars + 8u * (2 * ARES_SB + 4);
+    const uint32_t aempty_bar = bars + 8u * (2 * ARES_SB + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * ARES_SB + 6));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int num_k = cdiv(K, BK);
+    const int tiles_n = cdiv(N, BN);
+    const int tiles_m = cdiv(M, BM);
+    const int units = tiles_m * groups;
+    auto unit_range = [&](int u, int& m0, int& nt0, int& nt1) {
+        const int g = u % groups;
+        m0 = (u / groups) * BM;
+        nt0 = (int)(((long long)g * tiles_n) / groups);
+        nt1 = (int)(((long long)(g + 1) * tiles_n) / groups);
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ARES_SB; s++) {
+            mbar_init(bfull_bar(s), 1);
+            mbar_init(bempty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), EPI_WARPS);
+        }
+        mbar_init(afull_bar, 1);
+        mbar_init(aempty_bar, 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)(2 * TMEM_COLS))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int g = 0, ua = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x, ua++) {
+                int m0, nt0, nt1;
+                unit_range(u, m0, nt0, nt1);
+                if (ua >= 1 && !mbar_wait(aempty_bar, (ua - 1) & 1, abort_flag)) break;
+                mbar_expect_tx(afull_bar, (uint32_t)(num_k * BM * BK));
+                for (int k = 0; k < num_k; k++) tma_load_2d(a_base + k * BM * BK, &tmA, afull_bar, k * BK, m0);
+                for (int nt = nt0; nt < nt1 && ok; nt++) {
+                    for (int k = 0; k < num_k; k++, g++) {
+                        const int s = g % ARES_SB;
+                        if (g >= ARES_SB && !mbar_wait(bempty_bar(s), ((g / ARES_SB) - 1) & 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        mbar_expect_tx(bfull_bar(s), (uint32_t)ARES_B_BYTES);
+                        tma_load_2d(b_base + s * ARES_B_BYTES, &tmB, bfull_bar(s), k * BK, nt * BN);
+                    }
+                }
+            }
+            if (*abort_flag) {
+                // let issued loads land before the CTA exits (bounded)
+                for (int j = (g > ARES_SB ? g - ARES_SB : 0); j < g; j++) {
+                    const long long t0 = clock64();
+                    while (!mbar_try(bfull_bar(j % ARES_SB), (j / ARES_SB) & 1) && clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
+                if (ua > 0) {
+                    const long long t0 = clock64();
+                    while (!mbar_try(afull_bar, (ua - 1) & 1) && clock64() - t0 < WAIT_CYCLES) {
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = idesc_i8<BN>();
+            int g = 0, it = 0, ua = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ua++) {
+                int m0, nt0, nt1;
+                unit_range(u, m0, nt0, nt1);
+                if (!mbar_wait(afull_bar, ua & 1, abort_flag)) break;
+                tc_fence_after();
+                for (int nt = nt0; nt < nt1 && ok; nt++, it++) {
+                    const int a = it & 1;
+                    if (it >= 2 && !mbar_wait(tempty_bar(a), ((it >> 1) - 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t tacc = tmem + (uint32_t)(a * TMEM_COLS);
+                    for (int k = 0; k < num_k; k++, g++) {
+                        const int s = g % ARES_SB;
+                        if (!mbar_wait(bfull_bar(s), (g / ARES_SB) & 1, abort_flag)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = a_base + k * BM * BK;
+                        const uint32_t sb = b_base + s * ARES_B_BYTES;
+#pragma unroll
+                        for (int kk = 0; kk < BK / 32; kk++)
+                            mma_i8(tacc, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc, (k | kk) != 0);
+                        mma_commit(bempty_bar(s));
+                    }
+                    if (!ok) break;
+                    mma_commit(tfull_bar(a));
+                }
+                if (!ok) break;
+                mma_commit(aempty_bar);  // the unit's MMAs have all read A once they complete
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5), as in gemm_i8_kernel ----------------
+        const int q = warp & 3;
+        const uint32_t stg = stg_base + (uint32_t)((warp - 2) * ARES_STG * 4096);
+        unsigned char* stg_g = gbase + (stg - base);
+        const float ws = (epi == MI_EPI_F32_SCALED) ? *w_scale : 0.0f;
+        const float os = out_scale ? *out_scale : 1.0f;
+        int it = 0, nst = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            int m0, nt0, nt1;
+            unit_range(u, m0, nt0, nt1);
+            const int row = m0 + q * 32 + lane;
+            float sc = 0.0f;
+            if (epi == MI_EPI_F32_SCALED && row < M) sc = __fmul_rn(ws, a_scale[row]);  // (w_scale * x_scale)
+            for (int nt = nt0; nt < nt1; nt++, it++) {
+                const int a = it & 1;
+                if (!__all_sync(0xffffffffu, mbar_wait(tfull_bar(a), (it >> 1) & 1, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int n0 = nt * BN;
+                const uint32_t tacc = tmem + (uint32_t)(a * TMEM_COLS) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+                for (int cb = 0; cb < EPI_BOXES; cb++, nst++) {
+                    uint32_t r[32];
+                    tmem_ld16(tacc + (uint32_t)(cb * 32), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                    tmem_ld16(tacc + (uint32_t)(cb * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                    if (cb == EPI_BOXES - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(tempty_bar(a)) : "memory");
+                    }
+                    if (epi == MI_EPI_F32_SCALED) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            float v = __fmul_rn((float)(int32_t)r[j], sc);
+                            if (out_scale) v = __fmul_rn(v, os);
+                            r[j] = __float_as_uint(v);
+                        }
+                    }
+                    static_assert(ARES_STG == 2, "wait_group.read count below");
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;\n" ::: "memory");
+                    __syncwarp();
+                    unsigned char* rowp = stg_g + (nst & (ARES_STG - 1)) * 4096 + lane * 128;
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        const int phys = c ^ (lane & 7);
+                        *reinterpret_cast<uint4*>(rowp + phys * 16) =
+                            make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int x = n0 + cb * 32, y = m0 + q * 32;
+                        if (x < N && y < M) tma_store_2d(&tmC, stg + (nst & (ARES_STG - 1)) * 4096, x, y);
+                        asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+                    }
+                }
+            }
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                     "r"((uint32_t)(2 * TMEM_COLS))
+                     : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
@@ -393,6 +628,43 @@ static int launch(const int8_t* A, int lda, const int8_t* W, const float* a_scal
     return MI_OK;
 }
 
+static int sm_count() {
+    static int num_sms = 0;
+    if (!num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (num_sms <= 0) num_sms = 148;
+    }
+    return num_sms;
+}
+
+static int launch_ares(const int8_t* A, int lda, const int8_t* W, const float* a_scale, const float* w_scale,
+                       const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
+    CUtensorMap ta, tb, tc;
+    int rc = make_tmap(&ta, A, M, K, lda, BK, BM, 1);
+    if (rc) return rc;
+    rc = make_tmap(&tb, W, N, K, K, BK, ARES_BN, 1);
+    if (rc) return rc;
+    rc = make_tmap(&tc, out, M, N, (long long)ldo * 4, 32, 32, 4);
+    if (rc) return rc;
+    if (cudaFuncSetAttribute(gemm_i8_ares_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ARES_SMEM) !=
+        cudaSuccess)
+        return MI_ERR_CUDA;
+    const int sms = sm_count();
+    const int tiles_m = cdiv(M, BM), tiles_n = cdiv(N, ARES_BN);
+    // split each M tile's N range into groups until there are >= 2 units per SM
+    int groups = cdiv(2 * sms, tiles_m);
+    if (groups < 1) groups = 1;
+    if (groups > tiles_n) groups = tiles_n;
+    const int units = tiles_m * groups;
+    const int grid = units < sms ? units : sms;
+    gemm_i8_ares_kernel<<<grid, THREADS, ARES_SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M, N, K, epi,
+                                                         groups);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
 }  // namespace gemm
 }  // namespace mi
 
@@ -410,6 +682,8 @@ extern "C" int mi_bitlinear_i8(const int8_t* A, int lda, const int8_t* W, const 
     if (((uintptr_t)out) & 15) return MI_ERR_INVALID;
     if (K > 132104) return MI_ERR_UNSUPPORTED;
     cudaStream_t s = (cudaStream_t)stream;
+    if (K <= ARES_MAXK * BK && N > 128)  // wide outputs over a short K: keep A resident
+        return launch_ares(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (N <= 128 && N % 16 == 0 && N != 128) {
         // narrow projections (x_proj: N = dt_rank + 2*d_state) in one N tile
         if (N <= 32) return launch<32>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);

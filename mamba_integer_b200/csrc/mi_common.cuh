@@ -96,6 +96,32 @@ __device__ __forceinline__ float squareplus(float x) {
     return __fmul_rn(0.5f, __fadd_rn(x, s));
 }
 
+// squareplus of an argument known to satisfy |x| <= 999 or to be NaN: then
+// x*x + 4 lies in [4, 1e6] or is NaN, and the two clamps to [1e-6, 1e6] in
+// front of the Newton iteration are identities, so they are skipped.  Same
+// result as squareplus() for every such argument.  The outputs of
+// ste_clamp(., -50, 50) and ste_clamp(., -20, 20) qualify: x + (c - x)
+// differs from c by at most half an ulp of x, and when that exceeds the bound
+// the difference c - x rounds to -x and the result is 0, so the magnitude
+// never exceeds 2 * 50.
+__device__ __forceinline__ float squareplus_bounded(float x) {
+    const float y = __fadd_rn(__fmul_rn(x, x), 4.0f);
+    float r = (y > 16.0f) ? 0.125f : 0.5f;
+    r = (y > 64.0f) ? 0.0625f : r;
+    r = (y > 256.0f) ? 0.03125f : r;
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        float t = __fmul_rn(0.5f, y);
+        t = __fmul_rn(t, r);
+        t = __fmul_rn(t, r);
+        t = __fsub_rn(1.5f, t);
+        r = __fmul_rn(r, t);
+        r = clamp_t(r, 1e-6f, 1e3f);
+    }
+    const float s = clamp_t(__fmul_rn(y, r), 0.0f, 1e3f);
+    return __fmul_rn(0.5f, __fadd_rn(x, s));
+}
+
 // y * _sigmoid_algebraic(z) = y * (0.5 + (0.5*z) / (1 + |z|))  (:124-132, :444)
 __device__ __forceinline__ float sigmoid_gate(float y, float z) {
     float num = __fmul_rn(0.5f, z);

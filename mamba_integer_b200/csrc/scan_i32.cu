@@ -8,68 +8,62 @@
 // right shift, add) with the selective-scan input term B_t*x_t and the output
 // contraction C_t.h_t added.
 //
-// Layout / parallelism: one CTA per (batch row b, block of 64 channels); two
-// threads per channel, each holding 8 of the 16 states in registers for the
-// whole sequence (the recurrence is sequential in t).  x, B and C are staged
-// through a 3-deep shared-memory ring of 32-step chunks with cp.async so the
-// HBM reads run ahead of the arithmetic; y is combined across the two halves
-// with one shuffle and written per step.  n stays in registers.
+// Layout / parallelism: one warp per CTA owns 16 channels of one sequence;
+// two lanes per channel each hold 8 of the 16 int32 states in registers for
+// the whole sequence (the recurrence is sequential in t).  x and B|C arrive
+// through a per-warp double-buffered cp.async ring of TC-step chunks (no
+// block-level barriers); the two half sums of y meet with one shuffle, y is
+// staged in shared memory and written as 16-byte vectors.  n stays in
+// registers.
 //
 // Exactness: the shifted product fits int32 whenever 0 <= n <= 2^k (so the
 // 64-bit shift result is truncated losslessly); |B*x| < 2^30 when
-// |B|,|x| <= 32767; the state add is checked for int32 overflow with a
-// sign test, y is accumulated in 64 bits.  Violations set the device error
-// word instead of producing wrong values silently.
+// |B|,|x| <= 32767; the state add is checked for int32 overflow with a sign
+// test and y is accumulated in 64 bits.  Violations set the device error word
+// instead of producing wrong values silently.
 #include "mi_common.cuh"
 
 namespace mi {
 namespace scan_i32 {
 
-constexpr int CH = 64;          // channels per CTA
-constexpr int THREADS = 2 * CH; // two state halves per channel
-constexpr int TC = 32;          // time steps per staged chunk
-constexpr int STAGES = 3;
-constexpr int NS = 16;          // d_state
+constexpr int CH = 16;       // channels per warp
+constexpr int THREADS = 32;  // two lanes per channel
+constexpr int TC = 16;       // time steps per staged chunk
+constexpr int NS = 16;       // d_state
 constexpr int HALF = NS / 2;
 
-struct Smem {
-    int32_t x[STAGES][TC][CH];
-    int32_t bc[STAGES][TC][2 * NS];  // B[0..15] | C[0..15]
+struct Stage {
+    int32_t x[TC][CH];
+    int32_t bc[TC][2 * NS];  // B[0..15] | C[0..15]
 };
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
-    unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-    int sz = pred ? 16 : 0;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(sz));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(pred ? 16 : 0)
+                 : "memory");
 }
 
-// Stage chunk `c` (steps [c*TC, c*TC+TC)) of x[b, :, d0:d0+CH] and B/C[b, :, :].
-__device__ __forceinline__ void load_chunk(Smem& sm, int stage, int c, const int32_t* __restrict__ x,
+// Stage chunk [t0, t0+TC) of x[b, :, d0:d0+CH] and B|C[b, :, :].
+__device__ __forceinline__ void load_chunk(Stage& st, int t0, const int32_t* __restrict__ x,
                                            const int32_t* __restrict__ Bm, const int32_t* __restrict__ Cm,
-                                           int b, int d0, int L, int D) {
-    const int tid = threadIdx.x;
-    // x: TC rows x CH int32 = TC*16 chunks of 16 B
-    for (int i = tid; i < TC * (CH / 4); i += THREADS) {
-        int r = i / (CH / 4), q = i % (CH / 4);
-        int t = c * TC + r;
-        int d = d0 + q * 4;
-        bool ok = (t < L) && (d < D);
-        const int32_t* src = ok ? x + ((size_t)b * L + t) * D + d : x;
-        cp_async16(&sm.x[stage][r][q * 4], src, ok);
+                                           size_t row0, int d0, int L, int D) {
+    const int lane = threadIdx.x;
+#pragma unroll
+    for (int i = lane; i < TC * (CH / 4); i += 32) {  // x: TC rows x 4 chunks
+        const int r = i >> 2, q = i & 3;
+        const int t = t0 + r;
+        const bool ok = (t < L) && (d0 + 4 * q < D);
+        const int32_t* src = ok ? x + (row0 + t) * D + d0 + 4 * q : x;
+        cp_async16(&st.x[r][4 * q], src, ok);
     }
-    // B and C: TC rows x 16 int32 each = 4 chunks per row per matrix
-    for (int i = tid; i < TC * 8; i += THREADS) {
-        int r = i / 8, q = i % 8;
-        int t = c * TC + r;
-        bool ok = t < L;
+#pragma unroll
+    for (int i = lane; i < TC * 8; i += 32) {  // B|C: TC rows x 8 chunks
+        const int r = i >> 3, q = i & 7;
+        const int t = t0 + r;
+        const bool ok = t < L;
         const int32_t* base = (q < 4) ? Bm : Cm;
-        const int32_t* src = ok ? base + ((size_t)b * L + t) * NS + (q & 3) * 4 : base;
-        cp_async16(&sm.bc[stage][r][(q >> 2) * NS + (q & 3) * 4], src, ok);
+        const int32_t* src = ok ? base + (row0 + t) * NS + (q & 3) * 4 : base;
+        cp_async16(&st.bc[r][4 * q], src, ok);
     }
 }
 
@@ -78,89 +72,109 @@ __global__ void __launch_bounds__(THREADS)
 scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, const int32_t* __restrict__ Cm,
                 const int32_t* __restrict__ n, int k, int32_t* __restrict__ y32, int64_t* __restrict__ y64,
                 int32_t* __restrict__ h_io, int L, int D) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
+    __shared__ __align__(16) Stage stage[2];
+    __shared__ __align__(16) int64_t ys[TC][CH];
+    const int lane = threadIdx.x;
     const int b = blockIdx.y;
     const int d0 = blockIdx.x * CH;
-    const int tid = threadIdx.x;
-    const int ch = tid >> 1;         // channel within the CTA
-    const int half = tid & 1;        // which 8 states
+    const int ch = lane >> 1;   // channel within the warp
+    const int half = lane & 1;  // which 8 states
     const int d = d0 + ch;
     const bool active = d < D;
+    const size_t row0 = (size_t)b * L;
 
-    int32_t h[HALF];
-    int32_t nn[HALF];
+    int32_t h[HALF], nn[HALF];
     int bad = 0;
     const int32_t lim = 1 << k;
 #pragma unroll
     for (int j = 0; j < HALF; j++) {
-        int jj = half * HALF + j;
+        const int jj = half * HALF + j;
         h[j] = active ? h_io[((size_t)b * D + d) * NS + jj] : 0;
         nn[j] = active ? n[(size_t)d * NS + jj] : 0;
         bad |= (nn[j] < 0) | (nn[j] > lim);
     }
 
+    int ovf = 0;  // sign-test accumulator: negative => an int32 state or y32 overflowed
     const int nchunks = cdiv(L, TC);
-#pragma unroll
-    for (int s = 0; s < STAGES - 1; s++) {
-        if (s < nchunks) load_chunk(sm, s, s, x, Bm, Cm, b, d0, L, D);
-        cp_async_commit();
-    }
-
-    int ovf = 0;  // sign-test accumulator: negative => an int32 state overflowed
+    load_chunk(stage[0], 0, x, Bm, Cm, row0, d0, L, D);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
     for (int c = 0; c < nchunks; c++) {
-        // keep STAGES-1 chunks in flight
-        int cn = c + STAGES - 1;
-        if (cn < nchunks) load_chunk(sm, cn % STAGES, cn, x, Bm, Cm, b, d0, L, D);
-        cp_async_commit();
-        cp_async_wait<STAGES - 1>();
-        __syncthreads();
-        const int st = c % STAGES;
-        // range check of the staged inputs (cheap: a few values per thread per chunk)
-        for (int i = tid; i < TC * CH; i += THREADS) {
-            int32_t v = (&sm.x[st][0][0])[i];
+        Stage& st = stage[c & 1];
+        if (c + 1 < nchunks) load_chunk(stage[(c + 1) & 1], (c + 1) * TC, x, Bm, Cm, row0, d0, L, D);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        __syncwarp();
+        // range check of the staged inputs: 24 values per lane per chunk
+#pragma unroll
+        for (int i = lane; i < TC * CH; i += 32) {
+            const int32_t v = (&st.x[0][0])[i];
             bad |= (v < -32767) | (v > 32767);
         }
-        for (int i = tid; i < TC * 2 * NS; i += THREADS) {
-            int32_t v = (&sm.bc[st][0][0])[i];
+#pragma unroll
+        for (int i = lane; i < TC * 2 * NS; i += 32) {
+            const int32_t v = (&st.bc[0][0])[i];
             bad |= (v < -32767) | (v > 32767);
         }
-        const int tmax = min(TC, L - c * TC);
-        for (int r = 0; r < tmax; r++) {
-            const int32_t xv = sm.x[st][r][ch];
-            const int32_t* Bv = &sm.bc[st][r][half * HALF];
-            const int32_t* Cv = &sm.bc[st][r][NS + half * HALF];
-            int4 b0 = *reinterpret_cast<const int4*>(Bv);
-            int4 b1 = *reinterpret_cast<const int4*>(Bv + 4);
-            int4 c0 = *reinterpret_cast<const int4*>(Cv);
-            int4 c1 = *reinterpret_cast<const int4*>(Cv + 4);
+        const int t0 = c * TC;
+        const int tn = min(TC, L - t0);
+#pragma unroll 2
+        for (int r = 0; r < tn; r++) {
+            const int32_t xv = st.x[r][ch];
+            const int4 b0 = *reinterpret_cast<const int4*>(&st.bc[r][half * HALF]);
+            const int4 b1 = *reinterpret_cast<const int4*>(&st.bc[r][half * HALF + 4]);
+            const int4 c0 = *reinterpret_cast<const int4*>(&st.bc[r][NS + half * HALF]);
+            const int4 c1 = *reinterpret_cast<const int4*>(&st.bc[r][NS + half * HALF + 4]);
             const int32_t bb[HALF] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
             const int32_t cc[HALF] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            long long acc = 0;
+            // the 8 state chains are independent; the integer sums below are exact
+            // in any order, so they are formed as trees to keep dependency chains short
+            long long prod[HALF];
+            int32_t ov[HALF];
 #pragma unroll
             for (int j = 0; j < HALF; j++) {
-                long long p = (long long)h[j] * (long long)nn[j];
-                int32_t s = (int32_t)(p >> k);
-                int32_t bx = (int32_t)((uint32_t)bb[j] * (uint32_t)xv);  // |B*x| < 2^30 when in range
-                int32_t hn = (int32_t)((uint32_t)s + (uint32_t)bx);
-                ovf |= (s ^ hn) & (bx ^ hn);
+                const long long p = (long long)h[j] * (long long)nn[j];
+                const int32_t s = (int32_t)(p >> k);
+                const int32_t bx = (int32_t)((uint32_t)bb[j] * (uint32_t)xv);  // |B*x| < 2^30 when in range
+                const int32_t hn = (int32_t)((uint32_t)s + (uint32_t)bx);
+                ov[j] = (s ^ hn) & (bx ^ hn);
                 h[j] = hn;
-                acc += (long long)cc[j] * (long long)hn;
+                prod[j] = (long long)cc[j] * (long long)hn;
             }
+            ovf |= ((ov[0] | ov[1]) | (ov[2] | ov[3])) | ((ov[4] | ov[5]) | (ov[6] | ov[7]));
+            long long acc = ((prod[0] + prod[1]) + (prod[2] + prod[3])) + ((prod[4] + prod[5]) + (prod[6] + prod[7]));
             acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            if (active && half == 0) {
-                size_t o = ((size_t)b * L + (size_t)c * TC + r) * D + d;
-                if (Y64) {
-                    y64[o] = acc;
-                } else {
-                    if (acc > INT32_MAX || acc < INT32_MIN) ovf |= INT32_MIN;
-                    y32[o] = (int32_t)acc;
+            if (half == 0) ys[r][ch] = acc;
+        }
+        __syncwarp();
+        // write the chunk's y rows: TC rows x CH values as 16-byte vectors
+        if (Y64) {
+            for (int i = lane; i < TC * (CH / 2); i += 32) {
+                const int r = i >> 3, q = i & 7;  // 8 chunks of two int64 per row
+                const int dq = d0 + 2 * q;
+                if (r < tn && dq < D) {
+                    int64_t* o = y64 + (row0 + t0 + r) * D + dq;
+                    *reinterpret_cast<longlong2*>(o) = make_longlong2(ys[r][2 * q], ys[r][2 * q + 1]);
+                }
+            }
+        } else {
+            for (int i = lane; i < TC * (CH / 4); i += 32) {
+                const int r = i >> 2, q = i & 3;  // 4 chunks of four int32 per row
+                const int dq = d0 + 4 * q;
+                if (r < tn && dq < D) {
+                    int32_t v[4];
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const long long a = ys[r][4 * q + e];
+                        if (a > INT32_MAX || a < INT32_MIN) ovf |= INT32_MIN;
+                        v[e] = (int32_t)a;
+                    }
+                    *reinterpret_cast<int4*>(y32 + (row0 + t0 + r) * D + dq) = make_int4(v[0], v[1], v[2], v[3]);
                 }
             }
         }
-        __syncthreads();  // stage st is refilled by the next iteration's load
+        __syncwarp();  // ys and the stage buffer are rewritten next iteration
     }
-    cp_async_wait<0>();
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 
     if (active) {
 #pragma unroll
@@ -182,19 +196,15 @@ extern "C" int mi_scan_i32(const int32_t* x, const int32_t* B, const int32_t* C,
     if (batch <= 0 || L <= 0 || D <= 0) return MI_ERR_INVALID;
     if (N != NS) return MI_ERR_UNSUPPORTED;
     if (k < 1 || k > 30) return MI_ERR_UNSUPPORTED;
-    if (D % 4 != 0) return MI_ERR_UNSUPPORTED;  // 16-byte staging of x rows
-    if (((uintptr_t)x | (uintptr_t)B | (uintptr_t)C) & 15) return MI_ERR_INVALID;
+    if (D % 4 != 0) return MI_ERR_UNSUPPORTED;  // 16-byte staging of x rows and vector y stores
+    if (((uintptr_t)x | (uintptr_t)B | (uintptr_t)C | (uintptr_t)y32 | (uintptr_t)y64) & 15) return MI_ERR_INVALID;
     if (batch > 65535) return MI_ERR_UNSUPPORTED;
     dim3 grid(mi::cdiv(D, CH), batch);
-    size_t smem = sizeof(Smem);
     cudaStream_t s = (cudaStream_t)stream;
-    if (y64) {
-        cudaFuncSetAttribute(scan_i32_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        scan_i32_kernel<true><<<grid, THREADS, smem, s>>>(x, B, C, n, k, nullptr, y64, h_io, L, D);
-    } else {
-        cudaFuncSetAttribute(scan_i32_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        scan_i32_kernel<false><<<grid, THREADS, smem, s>>>(x, B, C, n, k, y32, nullptr, h_io, L, D);
-    }
+    if (y64)
+        scan_i32_kernel<true><<<grid, THREADS, 0, s>>>(x, B, C, n, k, nullptr, y64, h_io, L, D);
+    else
+        scan_i32_kernel<false><<<grid, THREADS, 0, s>>>(x, B, C, n, k, y32, nullptr, h_io, L, D);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

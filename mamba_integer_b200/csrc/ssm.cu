@@ -19,55 +19,70 @@ namespace ssm {
 // ---------------------------------------------------------------------------
 // conv + activation + quantisation
 // ---------------------------------------------------------------------------
-// One thread per (sequence, channel) walks a chunk of CONV_TC positions with the
-// 4-tap window in registers, so every input element is read once, coalesced
-// across channels.  The row absmax needed by the following int8 quantisation
-// is accumulated with one atomicMax per warp and position into amax (fp32
-// bits of non-negative values order like unsigned integers; NaN sorts above
-// +inf, which makes a NaN row propagate as torch.amax does).
+// One thread per (sequence, 4 adjacent channels) walks a chunk of CONV_TC
+// positions with the 4-tap windows in registers, so every input element is
+// read once with 16-byte loads, coalesced across channels.  The row absmax
+// needed by the following int8 quantisation is accumulated with one
+// atomicMax per warp and position into amax (fp32 bits of non-negative
+// values order like unsigned integers; NaN sorts above +inf, which makes a
+// NaN row propagate as torch.amax does).
 constexpr int CONV_THREADS = 128;
 constexpr int CONV_TC = 64;  // positions per CTA
 constexpr int CONV_G = 8;    // positions per group: computed together, absmax reduced together
 
-// xz: [batch*L, ldx], conv input = columns [0, D).  act: [batch*L, D].
+__device__ __forceinline__ float conv_tap4(float bs, float4 wc, float x0, float x1, float x2, float x3) {
+    // bias first, then one FMA per tap k = 0..3 over positions t-3+k
+    float acc = bs;
+    acc = __fmaf_rn(wc.x, x0, acc);
+    acc = __fmaf_rn(wc.y, x1, acc);
+    acc = __fmaf_rn(wc.z, x2, acc);
+    acc = __fmaf_rn(wc.w, x3, acc);
+    return squareplus_bounded(ste_clamp(acc, -50.0f, 50.0f));
+}
+
+// xz: [batch*L, ldx], conv input = columns [0, D).  act: [batch*L, D].  D % 4 == 0.
 __global__ void __launch_bounds__(CONV_THREADS)
 conv_act_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w, const float* __restrict__ bias,
                 float* __restrict__ act, unsigned int* __restrict__ amax, int L, int D) {
-    const int c = blockIdx.x * CONV_THREADS + threadIdx.x;
+    const int c = 4 * (blockIdx.x * CONV_THREADS + threadIdx.x);  // first of this thread's 4 channels
     const int lane = threadIdx.x & 31;
     const int b = blockIdx.y;
     const int t0 = blockIdx.z * CONV_TC;
     const bool active = c < D;
     const int cc = active ? c : 0;
-    const float4 wc = *reinterpret_cast<const float4*>(w + 4 * cc);
-    const float bs = bias[cc];
+    float4 wv[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) wv[e] = *reinterpret_cast<const float4*>(w + 4 * (cc + e));
+    const float4 bs = *reinterpret_cast<const float4*>(bias + cc);
     const size_t row0 = (size_t)b * L;
     const float* px = xz + row0 * ldx + cc;
-    // window x[t-3], x[t-2], x[t-1]
-    float w0 = (t0 - 3 >= 0) ? px[(size_t)(t0 - 3) * ldx] : 0.0f;
-    float w1 = (t0 - 2 >= 0) ? px[(size_t)(t0 - 2) * ldx] : 0.0f;
-    float w2 = (t0 - 1 >= 0) ? px[(size_t)(t0 - 1) * ldx] : 0.0f;
+    const float4 zero4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    // windows x[t-3], x[t-2], x[t-1] of the 4 channels
+    float4 w0 = (t0 - 3 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 3) * ldx) : zero4;
+    float4 w1 = (t0 - 2 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 2) * ldx) : zero4;
+    float4 w2 = (t0 - 1 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 1) * ldx) : zero4;
     const int tend = min(L, t0 + CONV_TC);
     for (int t = t0; t < tend; t += CONV_G) {
-        float xv[CONV_G];
+        float4 xv[CONV_G];
 #pragma unroll
-        for (int j = 0; j < CONV_G; j++) xv[j] = (t + j < tend) ? __ldg(px + (size_t)(t + j) * ldx) : 0.0f;
+        for (int j = 0; j < CONV_G; j++)
+            xv[j] = (t + j < tend) ? __ldg(reinterpret_cast<const float4*>(px + (size_t)(t + j) * ldx)) : zero4;
         unsigned m[CONV_G];
 #pragma unroll
         for (int j = 0; j < CONV_G; j++) {
-            // bias first, then one FMA per tap k = 0..3 over positions t-3+k
-            float acc = bs;
-            acc = __fmaf_rn(wc.x, w0, acc);
-            acc = __fmaf_rn(wc.y, w1, acc);
-            acc = __fmaf_rn(wc.z, w2, acc);
-            acc = __fmaf_rn(wc.w, xv[j], acc);
+            float4 a;
+            a.x = conv_tap4(bs.x, wv[0], w0.x, w1.x, w2.x, xv[j].x);
+            a.y = conv_tap4(bs.y, wv[1], w0.y, w1.y, w2.y, xv[j].y);
+            a.z = conv_tap4(bs.z, wv[2], w0.z, w1.z, w2.z, xv[j].z);
+            a.w = conv_tap4(bs.w, wv[3], w0.w, w1.w, w2.w, xv[j].w);
             w0 = w1;
             w1 = w2;
             w2 = xv[j];
-            const float a = squareplus(ste_clamp(acc, -50.0f, 50.0f));
             const bool ok = active && (t + j < tend);
-            if (ok) act[(row0 + t + j) * D + c] = a;
-            m[j] = ok ? __float_as_uint(fabsf(a)) : 0u;
+            if (ok) *reinterpret_cast<float4*>(act + (row0 + t + j) * D + c) = a;
+            const unsigned mx = max(max(__float_as_uint(fabsf(a.x)), __float_as_uint(fabsf(a.y))),
+                                    max(__float_as_uint(fabsf(a.z)), __float_as_uint(fabsf(a.w))));
+            m[j] = ok ? mx : 0u;
         }
         // row absmax of the group's positions: butterflies interleaved over the group
 #pragma unroll
@@ -126,15 +141,15 @@ struct DtSource {
 };
 
 // Issue the cp.async copies of chunk [t0, t0+SC) into `st` (16-byte copies).
-template <int RW>
+template <int RW, int CHW>
 __device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __restrict__ act, const DtSource& src,
                                                 const float* __restrict__ z, const float* __restrict__ bc, int ldbc,
                                                 int ldz, size_t row0, int t0, int L, int d0, int D) {
     const int lane = threadIdx.x & 31;
+    constexpr int QR = CHW / 4;  // 16-byte chunks per row of the warp's channels
 #pragma unroll
-    for (int h2 = 0; h2 < SC * 8 / 32; h2++) {
-        const int idx = lane + 32 * h2;  // 16-byte chunk: step r, quarter q
-        const int r = idx >> 3, q = idx & 7;
+    for (int idx = lane; idx < SC * QR; idx += 32) {  // step r, quarter q
+        const int r = idx / QR, q = idx % QR;
         const int t = t0 + r;
         const bool okt = t < L;
         const bool ok = okt && (d0 + 4 * q < D);
@@ -143,12 +158,20 @@ __device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __re
         cp_async16(&st.act[r][4 * q], act + row * D + c, ok);
         if (RW == 0) cp_async16(&st.mod[r][4 * q], src.modraw + row * D + c, ok);
         cp_async16(&st.z[r][4 * q], z + row * ldz + c, ok);
-        cp_async16(&st.bc[r][4 * q], bc + row * ldbc + (okt ? 4 * q : 0), okt);
+    }
+#pragma unroll
+    for (int idx = lane; idx < SC * 8; idx += 32) {  // B|C rows: 8 chunks each
+        const int r = idx >> 3, q = idx & 7;
+        const int t = t0 + r;
+        const bool okt = t < L;
+        const size_t row = row0 + (okt ? t : 0);
+        cp_async16(&st.bc[r][4 * q], bc + row * ldbc + 4 * q, okt);
     }
     if (RW > 0) {
         // dt rows: SC rows x (RW/4) chunks of 16 bytes; scales: SC x 4 bytes
-        for (int idx = lane; idx < SC * (RW / 4); idx += 32) {
-            const int r = idx / (RW / 4), q = idx % (RW / 4);
+        constexpr int RQ = RW > 0 ? RW / 4 : 1;
+        for (int idx = lane; idx < SC * RQ; idx += 32) {
+            const int r = idx / RQ, q = idx % RQ;
             const int t = t0 + r;
             const bool okt = t < L;
             const size_t row = row0 + (okt ? t : 0);
@@ -161,31 +184,38 @@ __device__ __forceinline__ void scan_stage_load(ScanStage& st, const float* __re
     }
 }
 
-// One warp owns 32 channels of one sequence; each lane carries its channel's
-// 16 fp32 states in registers for the whole sequence.  Inputs arrive through
-// a per-warp double-buffered cp.async ring of SC-step chunks (no block-level
-// barriers).  Each chunk is processed in three phases so that only the state
-// recurrence is serial: (A) decay clamp / dt / x*dt for SC steps, (B) the
-// 16-state convex update and h.C per step, (C) gates, stores and the row
-// absmax reductions for SC steps at once.
+// One warp owns 32/S channels of one sequence; the S lanes of a channel each
+// carry 16/S of its fp32 states in registers for the whole sequence (S = 1
+// when the layer has enough (sequence, channel) pairs to fill the GPU, 2 or 4
+// for small per-GPU batches).  Inputs arrive through a per-warp
+// double-buffered cp.async ring of SC-step chunks (no block-level barriers).
+// Each chunk is processed in three phases so that only the state recurrence
+// is serial: (A) decay clamp / dt / x*dt for SC steps, (B) the convex state
+// update and h.C per step, (C) gates, stores and the row absmax reductions for
+// SC steps at once.  With S > 1 the h.C accumulation keeps its n = 0..15
+// order by continuing the fused multiply-add chain lane after lane.
 //
 // RW > 0 fuses the dt_proj BitLinear: each lane keeps its channel's ternary
 // dt_proj weights (4*RW int8) in registers and forms the exact int32 dot
 // product with the step's quantised dt row by dp4a, then applies the
 // BitLinear rescale acc * (w_scale * dt_scale[t]) exactly as the GEMM
 // epilogue does (src/rational_bitnet.py:204-208).
-// (22 one-warp CTAs per SM by registers and shared memory: all 3072 CTAs of a
+// (21 one-warp CTAs per SM by registers and shared memory: all 3072 CTAs of a
 // 64-sequence x 1536-channel layer are resident at once.)
-template <int RW>
-__global__ void __launch_bounds__(SCAN_THREADS, 22)
+template <int RW, int S>
+__global__ void __launch_bounds__(SCAN_THREADS, 21)
 ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
                 const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
                 float* __restrict__ amax, int L, int D) {
+    constexpr int CHW = 32 / S;   // channels per warp
+    constexpr int NSL = NS / S;   // states per lane
     __shared__ __align__(16) ScanStage stage[SSTAGES];
     const int lane = threadIdx.x;
+    const int ch = lane / S;      // channel within the warp
+    const int sub = lane % S;     // which slice of the 16 states
     const int b = blockIdx.y;
-    const int d0 = blockIdx.x * 32;
-    const int d = d0 + lane;
+    const int d0 = blockIdx.x * CHW;
+    const int d = d0 + ch;
     const bool active = d < D;
     const int dd = active ? d : 0;
     const size_t row0 = (size_t)b * L;
@@ -202,32 +232,34 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
         wsc = *src.w_scale;
     }
 
-    // states and base / 2^15 in pairs for the packed f32x2 arithmetic
-    float2 h2[NS / 2], bs2[NS / 2];
+    // this lane's states and base / 2^15; the fast-path bounds use all 16 bases
+    float h[NSL], bsl[NSL];
     float bmin = __int_as_float(0x7f800000), bmax = -__int_as_float(0x7f800000);
     bool bnan = false;
 #pragma unroll
-    for (int i = 0; i < NS / 2; i++) {
-        const float b0 = base[(size_t)dd * NS + 2 * i], b1 = base[(size_t)dd * NS + 2 * i + 1];
-        bs2[i] = make_float2(__fmul_rn(b0, 3.0517578125e-05f), __fmul_rn(b1, 3.0517578125e-05f));
-        h2[i] = make_float2(0.0f, 0.0f);
-        bmin = fminf(bmin, fminf(b0, b1));
-        bmax = fmaxf(bmax, fmaxf(b0, b1));
-        bnan |= (b0 != b0) | (b1 != b1);
+    for (int n = 0; n < NS; n++) {
+        const float bv = base[(size_t)dd * NS + n];
+        bmin = fminf(bmin, bv);
+        bmax = fmaxf(bmax, bv);
+        bnan |= (bv != bv);
+        if (n / NSL == sub) bsl[n % NSL] = __fmul_rn(bv, 3.0517578125e-05f);
     }
+#pragma unroll
+    for (int i = 0; i < NSL; i++) h[i] = 0.0f;
 
     const int nchunks = cdiv(L, SC);
-    scan_stage_load<RW>(stage[0], act, src, z, bc, ldbc, ldz, row0, 0, L, d0, D);
+    scan_stage_load<RW, CHW>(stage[0], act, src, z, bc, ldbc, ldz, row0, 0, L, d0, D);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     for (int c = 0; c < nchunks; c++) {
         ScanStage& st = stage[c & 1];
         if (c + 1 < nchunks)
-            scan_stage_load<RW>(stage[(c + 1) & 1], act, src, z, bc, ldbc, ldz, row0, (c + 1) * SC, L, d0, D);
+            scan_stage_load<RW, CHW>(stage[(c + 1) & 1], act, src, z, bc, ldbc, ldz, row0, (c + 1) * SC, L, d0, D);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
         __syncwarp();
         const int t0 = c * SC;
         const int tn = min(SC, L - t0);
+        float modr[SC];
         if (RW > 0) {
             // decay_mod before its clamp = dt_proj(dt): exact int32 dot product of the
             // int8 dt row with the ternary weights, then acc * (w_scale * dt_scale)
@@ -243,90 +275,102 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
                     acc = __dp4a(qv.z, wd[4 * k + 2], acc);
                     acc = __dp4a(qv.w, wd[4 * k + 3], acc);
                 }
-                st.mod[j][lane] = __fmul_rn((float)acc, __fmul_rn(wsc, st.dts[j]));
+                modr[j] = __fmul_rn((float)acc, __fmul_rn(wsc, st.dts[j]));
             }
+        } else {
+#pragma unroll
+            for (int j = 0; j < SC; j++) modr[j] = st.mod[j][ch];
         }
 
         // (A) per (step, channel): decay_mod, dt_val, x*dt   (:419-428)
         unsigned fast_mask = 0;
+        float xdtr[SC];
 #pragma unroll
         for (int j = 0; j < SC; j++) {
-            const float mod = ste_clamp(st.mod[j][lane], -20.0f, 20.0f);
-            const float dtv = ste_clamp(__fmul_rn(squareplus(mod), 0.01f), 0.001f, 0.1f);
-            st.mod[j][lane] = mod;
-            st.act[j][lane] = __fmul_rn(st.act[j][lane], dtv);  // x * dt_val
+            const float mod = ste_clamp(modr[j], -20.0f, 20.0f);
+            const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);
+            modr[j] = mod;
+            xdtr[j] = __fmul_rn(st.act[j][ch], dtv);  // x * dt_val
             // decay_nums = ste_clamp(v, 0, 32000), v = base + mod, equals the plain
             // clamp(v, 0, 32000) whenever v <= 64000: for v > 32000 the difference
             // 32000 - v is exact (Sterbenz) so v + (32000 - v) = 32000, for v < 0 it
             // gives +0, and inside the range it is the identity.  Rounding is monotone,
-            // so the channel's largest base decides.  base >= 1 and a mod that is 0 or
-            // not tiny keep base/2^15 and mod/2^15 exact (no subnormals), which the
-            // fast path below relies on.
-            const bool inside = !bnan && (bmin >= 1.0f) && (__fadd_rn(bmax, mod) <= 64000.0f) &&
-                                (mod == 0.0f || fabsf(mod) >= 1e-30f);
+            // so the channel's extreme bases decide.  base >= 1 and a mod that is 0 or
+            // not tiny keep base/2^15 and mod/2^15 exact (no subnormals), and with
+            // base + mod >= 0 for every state the lower bound cannot bind.
+            const bool inside = !bnan && (bmin >= 1.0f) && (__fadd_rn(bmin, mod) >= 0.0f) &&
+                                (__fadd_rn(bmax, mod) <= 64000.0f) && (mod == 0.0f || fabsf(mod) >= 1e-30f);
             if (__all_sync(0xffffffffu, inside)) fast_mask |= 1u << j;
+            if (S == 1) {  // each lane owns its column: write back at once (fewer live registers)
+                st.mod[j][ch] = modr[j];
+                st.act[j][ch] = xdtr[j];
+            }
         }
+        if (S > 1) {
+            __syncwarp();  // every lane of a channel has read act before one of them rewrites it
+            if (sub == 0) {
+#pragma unroll
+                for (int j = 0; j < SC; j++) {
+                    st.mod[j][ch] = modr[j];
+                    st.act[j][ch] = xdtr[j];
+                }
+            }
+        }
+        __syncwarp();
         // (B) the recurrence, one step at a time
 #pragma unroll 1
         for (int j = 0; j < tn; j++) {
-            const float mod = st.mod[j][lane];
-            const float xdt = st.act[j][lane];
-            const float2* B2 = reinterpret_cast<const float2*>(&st.bc[j][0]);
-            const float2* C2 = reinterpret_cast<const float2*>(&st.bc[j][NS]);
+            const float mod = st.mod[j][ch];
+            const float xdt = st.act[j][ch];
+            const float* Bv = &st.bc[j][sub * NSL];
+            const float* Cv = &st.bc[j][NS + sub * NSL];
             if (fast_mask & (1u << j)) {
                 // decay = clamp(base + mod, 0, 32000) / 2^15
-                //       = clamp(base/2^15 + mod/2^15, 0, 32000/2^15): both scalings are
+                //       = min(base/2^15 + mod/2^15, 32000/2^15): both scalings are
                 // exact, the sum rounds once, and scaling by 2^-15 commutes with
                 // rounding and with the clamp away from subnormals
                 const float ms = __fmul_rn(mod, 3.0517578125e-05f);
 #pragma unroll
-                for (int i = 0; i < NS / 2; i++) {
-                    const float2 bq = B2[i];
-                    float hv[2] = {h2[i].x, h2[i].y};
-                    const float bb[2] = {bs2[i].x, bs2[i].y}, Bq[2] = {bq.x, bq.y};
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const float dec = clamp_t(__fadd_rn(bb[e], ms), 0.0f, 0.9765625f);  // 32000 / 2^15
-                        const float u = __fmul_rn(xdt, Bq[e]);
-                        // h = h * decay + (1 - decay) * u                   (:309)
-                        hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
-                    }
-                    h2[i] = make_float2(hv[0], hv[1]);
+                for (int i = 0; i < NSL; i++) {
+                    const float dec = min_nan(__fadd_rn(bsl[i], ms), 0.9765625f);  // 32000 / 2^15
+                    const float u = __fmul_rn(xdt, Bv[i]);
+                    // h = h * decay + (1 - decay) * u                   (:309)
+                    h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < NS / 2; i++) {
-                    const float2 bq = B2[i];
-                    float hv[2] = {h2[i].x, h2[i].y};
-                    const float bb[2] = {bs2[i].x, bs2[i].y}, Bq[2] = {bq.x, bq.y};
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const float bn = __fmul_rn(bb[e], 32768.0f);  // exact: back to base
-                        const float num = ste_clamp(__fadd_rn(bn, mod), 0.0f, 32000.0f);
-                        const float dec = __fmul_rn(num, 3.0517578125e-05f);
-                        const float u = __fmul_rn(xdt, Bq[e]);
-                        hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
-                    }
-                    h2[i] = make_float2(hv[0], hv[1]);
+                for (int i = 0; i < NSL; i++) {
+                    const float bn = __fmul_rn(bsl[i], 32768.0f);  // exact: back to base
+                    const float num = ste_clamp(__fadd_rn(bn, mod), 0.0f, 32000.0f);
+                    const float dec = __fmul_rn(num, 3.0517578125e-05f);
+                    const float u = __fmul_rn(xdt, Bv[i]);
+                    h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
                 }
             }
-            // y = matmul(h, C[..., None]): fused multiply-add over n = 0..15 from 0   (:440)
+            // y = matmul(h, C[..., None]): fused multiply-add over n = 0..15 from 0   (:440);
+            // the chain passes from the lane holding states [s*NSL, ...) to the next
             float yacc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < NS / 2; i++) {
-                const float2 cq = C2[i];
-                yacc = __fmaf_rn(h2[i].x, cq.x, yacc);
-                yacc = __fmaf_rn(h2[i].y, cq.y, yacc);
+            for (int s = 0; s < S; s++) {
+                const float yin = (s == 0) ? 0.0f : __shfl_up_sync(0xffffffffu, yacc, 1);
+                if (sub == s) {
+                    yacc = yin;
+#pragma unroll
+                    for (int i = 0; i < NSL; i++) yacc = __fmaf_rn(h[i], Cv[i], yacc);
+                }
             }
-            st.mod[j][lane] = yacc;  // decay_mod of step j is no longer needed
+            __syncwarp();
+            if (sub == S - 1) st.mod[j][ch] = yacc;  // decay_mod of step j is no longer needed
         }
+        __syncwarp();
         // (C) gate, store, row absmax                                 (:441-444)
+        const bool owner = active && (sub == S - 1);
         unsigned m[SC];
 #pragma unroll
         for (int j = 0; j < SC; j++) {
-            const float out = sigmoid_gate(st.mod[j][lane], st.z[j][lane]);
-            if (j < tn && active) y[(row0 + t0 + j) * D + d] = out;
-            m[j] = (j < tn && active) ? __float_as_uint(fabsf(out)) : 0u;
+            const float out = sigmoid_gate(st.mod[j][ch], st.z[j][ch]);
+            if (j < tn && owner) y[(row0 + t0 + j) * D + d] = out;
+            m[j] = (j < tn && owner) ? __float_as_uint(fabsf(out)) : 0u;
         }
         if (amax) {
 #pragma unroll
@@ -383,6 +427,196 @@ static int ew_blocks(int64_t n) {
     return (int)(b < 1 ? 1 : b);
 }
 
+// Split-lane variant (S = 2 or 4 lanes per channel) for small per-GPU batches.
+// The S lanes of a channel share its work instead of repeating it:
+//   (A) the decay_mod / dt / x*dt prologue of step j is computed by lane
+//       j % S of the channel only (the fast-path vote becomes a ballot);
+//   (B1) each lane advances its 16/S states for every step and writes the
+//       state snapshot of each step to shared memory;
+//   (B2) the h.C contractions of the chunk (SC steps x 32/S channels) are
+//       spread over the warp, each a 16-term fused multiply-add chain in the
+//       reference order n = 0..15 read from the snapshots, so no shuffle sits
+//       on the per-step critical path;
+//   (C) the gate, store and row absmax of step j again by lane j % S.
+template <int RW, int S>
+__global__ void __launch_bounds__(SCAN_THREADS)
+ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
+                      const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
+                      float* __restrict__ amax, int L, int D) {
+    static_assert(S == 2 || S == 4, "split variant");
+    constexpr int CHW = 32 / S;   // channels per warp
+    constexpr int NSL = NS / S;   // states per lane
+    constexpr int SPL = SC / S;   // prologue / gate steps per lane
+    __shared__ __align__(16) ScanStage stage[SSTAGES];
+    __shared__ __align__(16) float snap[SC][32][NSL];
+    const int lane = threadIdx.x;
+    const int ch = lane / S;
+    const int sub = lane % S;
+    const int b = blockIdx.y;
+    const int d0 = blockIdx.x * CHW;
+    const int d = d0 + ch;
+    const bool active = d < D;
+    const int dd = active ? d : 0;
+    const size_t row0 = (size_t)b * L;
+    // lanes with the same sub-index: (lane % S == s) <=> bit pattern
+    constexpr unsigned SUBMASK0 = S == 2 ? 0x55555555u : 0x11111111u;
+
+    int32_t wd[RW > 0 ? RW : 1];
+    float wsc = 0.0f;
+    if (RW > 0) {
+        const int4* wrow = reinterpret_cast<const int4*>(src.w + (size_t)dd * (4 * RW));
+#pragma unroll
+        for (int k = 0; k < RW / 4; k++) {
+            const int4 v = wrow[k];
+            wd[4 * k] = v.x; wd[4 * k + 1] = v.y; wd[4 * k + 2] = v.z; wd[4 * k + 3] = v.w;
+        }
+        wsc = *src.w_scale;
+    }
+    float h[NSL], bsl[NSL];
+    float bmin = __int_as_float(0x7f800000), bmax = -__int_as_float(0x7f800000);
+    bool bnan = false;
+#pragma unroll
+    for (int n = 0; n < NS; n++) {
+        const float bv = base[(size_t)dd * NS + n];
+        bmin = fminf(bmin, bv);
+        bmax = fmaxf(bmax, bv);
+        bnan |= (bv != bv);
+        if (n / NSL == sub) bsl[n % NSL] = __fmul_rn(bv, 3.0517578125e-05f);
+    }
+#pragma unroll
+    for (int i = 0; i < NSL; i++) h[i] = 0.0f;
+
+    const int nchunks = cdiv(L, SC);
+    scan_stage_load<RW, CHW>(stage[0], act, src, z, bc, ldbc, ldz, row0, 0, L, d0, D);
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    for (int c = 0; c < nchunks; c++) {
+        ScanStage& st = stage[c & 1];
+        if (c + 1 < nchunks)
+            scan_stage_load<RW, CHW>(stage[(c + 1) & 1], act, src, z, bc, ldbc, ldz, row0, (c + 1) * SC, L, d0, D);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+        __syncwarp();
+        const int t0 = c * SC;
+        const int tn = min(SC, L - t0);
+
+        // (A) prologue of steps j = sub, sub + S, ... of this lane's channel   (:419-428)
+        unsigned fast_mask = 0;
+#pragma unroll
+        for (int k = 0; k < SPL; k++) {
+            const int j = sub + k * S;
+            float mr;
+            if (RW > 0) {
+                const int4* q4 = reinterpret_cast<const int4*>(&st.dtq[j][0]);
+                int acc = 0;
+#pragma unroll
+                for (int w4 = 0; w4 < RW / 4; w4++) {
+                    const int4 qv = q4[w4];
+                    acc = __dp4a(qv.x, wd[4 * w4], acc);
+                    acc = __dp4a(qv.y, wd[4 * w4 + 1], acc);
+                    acc = __dp4a(qv.z, wd[4 * w4 + 2], acc);
+                    acc = __dp4a(qv.w, wd[4 * w4 + 3], acc);
+                }
+                mr = __fmul_rn((float)acc, __fmul_rn(wsc, st.dts[j]));
+            } else {
+                mr = st.mod[j][ch];
+            }
+            const float mod = ste_clamp(mr, -20.0f, 20.0f);
+            const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);
+            st.act[j][ch] = __fmul_rn(st.act[j][ch], dtv);  // x * dt_val (this lane owns (j, ch))
+            st.mod[j][ch] = mod;
+            // same fast-path condition as the one-lane kernel (see there)
+            const bool inside = !active || (!bnan && (bmin >= 1.0f) && (__fadd_rn(bmin, mod) >= 0.0f) &&
+                                            (__fadd_rn(bmax, mod) <= 64000.0f) &&
+                                            (mod == 0.0f || fabsf(mod) >= 1e-30f));
+            const unsigned bal = __ballot_sync(0xffffffffu, inside);
+#pragma unroll
+            for (int s = 0; s < S; s++) {
+                const unsigned m = SUBMASK0 << s;
+                if ((bal & m) == m) fast_mask |= 1u << (s + k * S);
+            }
+        }
+        __syncwarp();
+        // (B1) state recurrence; snapshot of every step
+#pragma unroll 1
+        for (int j = 0; j < tn; j++) {
+            const float mod = st.mod[j][ch];
+            const float xdt = st.act[j][ch];
+            const float* Bv = &st.bc[j][sub * NSL];
+            if (fast_mask & (1u << j)) {
+                const float ms = __fmul_rn(mod, 3.0517578125e-05f);
+#pragma unroll
+                for (int i = 0; i < NSL; i++) {
+                    const float dec = min_nan(__fadd_rn(bsl[i], ms), 0.9765625f);  // 32000 / 2^15
+                    const float u = __fmul_rn(xdt, Bv[i]);
+                    // h = h * decay + (1 - decay) * u                   (:309)
+                    h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < NSL; i++) {
+                    const float bn = __fmul_rn(bsl[i], 32768.0f);  // exact: back to base
+                    const float num = ste_clamp(__fadd_rn(bn, mod), 0.0f, 32000.0f);
+                    const float dec = __fmul_rn(num, 3.0517578125e-05f);
+                    const float u = __fmul_rn(xdt, Bv[i]);
+                    h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < NSL; i += 4)
+                *reinterpret_cast<float4*>(&snap[j][lane][i]) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+        }
+        __syncwarp();
+        // (B2) y = matmul(h, C[..., None]): fused multiply-add over n = 0..15 from 0   (:440)
+#pragma unroll
+        for (int p = lane; p < SC * CHW; p += 32) {
+            const int j = p / CHW, cc = p % CHW;
+            if (j < tn) {
+                const float* hs = &snap[j][cc * S][0];  // the 16 states of channel cc, n ascending
+                const float* Cv = &st.bc[j][NS];
+                float yacc = 0.0f;
+#pragma unroll
+                for (int n = 0; n < NS; n += 4) {
+                    const float4 hq = *reinterpret_cast<const float4*>(hs + n);
+                    const float4 cq = *reinterpret_cast<const float4*>(Cv + n);
+                    yacc = __fmaf_rn(hq.x, cq.x, yacc);
+                    yacc = __fmaf_rn(hq.y, cq.y, yacc);
+                    yacc = __fmaf_rn(hq.z, cq.z, yacc);
+                    yacc = __fmaf_rn(hq.w, cq.w, yacc);
+                }
+                st.mod[j][cc] = yacc;  // decay_mod of step j is no longer needed
+            }
+        }
+        __syncwarp();
+        // (C) gate, store, row absmax of steps j = sub + k*S               (:441-444)
+        unsigned m[SPL];
+#pragma unroll
+        for (int k = 0; k < SPL; k++) {
+            const int j = sub + k * S;
+            const float out = sigmoid_gate(st.mod[j][ch], st.z[j][ch]);
+            const bool ok = active && j < tn;
+            if (ok) y[(row0 + t0 + j) * D + d] = out;
+            m[k] = ok ? __float_as_uint(fabsf(out)) : 0u;
+        }
+        if (amax) {
+            // reduce over the lanes of the same sub-index (xor offsets >= S keep it)
+#pragma unroll
+            for (int o = 16; o >= S; o >>= 1) {
+#pragma unroll
+                for (int k = 0; k < SPL; k++) m[k] = max(m[k], __shfl_xor_sync(0xffffffffu, m[k], o));
+            }
+            if (ch == 0) {
+#pragma unroll
+                for (int k = 0; k < SPL; k++) {
+                    const int j = sub + k * S;
+                    if (j < tn) atomicMax(reinterpret_cast<unsigned int*>(amax) + row0 + t0 + j, m[k]);
+                }
+            }
+        }
+        __syncwarp();  // the buffers are refilled by the next iteration
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
 }  // namespace ssm
 }  // namespace mi
 
@@ -392,18 +626,55 @@ extern "C" int mi_conv_act_quant(const float* xz, int ldx, const float* w, const
     if ((xq == nullptr) != (xscale == nullptr)) return MI_ERR_INVALID;
     if (xq && !amax_ws) return MI_ERR_INVALID;
     if (batch <= 0 || L <= 0 || D <= 0 || ldx < D) return MI_ERR_INVALID;
-    if (((uintptr_t)w) & 15) return MI_ERR_INVALID;
+    if (((uintptr_t)w | (uintptr_t)bias | (uintptr_t)xz | (uintptr_t)act) & 15) return MI_ERR_INVALID;
+    if ((D | ldx) & 3) return MI_ERR_UNSUPPORTED;  // 16-byte vectors of 4 channels
     if (batch > 65535 || mi::cdiv(L, mi::ssm::CONV_TC) > 65535) return MI_ERR_UNSUPPORTED;
     cudaStream_t s = (cudaStream_t)stream;
     const int T = batch * L;
     if (amax_ws && cudaMemsetAsync(amax_ws, 0, sizeof(float) * (size_t)T, s) != cudaSuccess) return MI_ERR_CUDA;
-    dim3 grid(mi::cdiv(D, mi::ssm::CONV_THREADS), batch, mi::cdiv(L, mi::ssm::CONV_TC));
+    dim3 grid(mi::cdiv(D, 4 * mi::ssm::CONV_THREADS), batch, mi::cdiv(L, mi::ssm::CONV_TC));
     mi::ssm::conv_act_kernel<<<grid, mi::ssm::CONV_THREADS, 0, s>>>(
         xz, ldx, w, bias, act, reinterpret_cast<unsigned int*>(amax_ws), L, D);
     MI_CHECK_LAUNCH();
     if (xq) return mi_quantize_rows(act, D, T, D, xq, D, xscale, amax_ws, stream);
     return MI_OK;
 }
+
+namespace mi {
+namespace ssm {
+
+// Lanes per channel: 1 when the layer's (sequence, channel) pairs give at
+// least 8 warps per SM, else 2 or 4 (small per-GPU batches).
+static int pick_split(int batch, int D) {
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    const long long want = 8LL * sms;
+    if ((long long)batch * cdiv(D, 32) >= want) return 1;
+    if ((long long)batch * cdiv(D, 16) >= want) return 2;
+    return 4;
+}
+
+template <int RW>
+static void launch_scan(int split, int batch, int L, int D, const float* act, const float* bc, int ldbc,
+                        const DtSource& src, const float* z, int ldz, const float* base, float* y, float* amax,
+                        cudaStream_t s) {
+    const int chw = SCAN_THREADS / split;
+    dim3 grid(cdiv(D, chw), batch);
+    if (split == 1)
+        ssm_scan_kernel<RW, 1><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, L, D);
+    else if (split == 2)
+        ssm_scan_split_kernel<RW, 2><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, L, D);
+    else
+        ssm_scan_split_kernel<RW, 4><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, L, D);
+}
+
+}  // namespace ssm
+}  // namespace mi
 
 extern "C" int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw, const float* z, int ldz,
                            const float* base, float* y, float* amax, int batch, int L, int D, int N, void* stream) {
@@ -414,20 +685,21 @@ extern "C" int mi_ssm_scan(const float* act, const float* bc, int ldbc, const fl
     // 16-byte asynchronous staging of rows
     if (((uintptr_t)act | (uintptr_t)bc | (uintptr_t)modraw | (uintptr_t)z) & 15) return MI_ERR_UNSUPPORTED;
     if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
-    dim3 grid(mi::cdiv(D, mi::ssm::SCAN_THREADS), batch);
     mi::ssm::DtSource src{modraw, nullptr, 0, nullptr, nullptr, nullptr};
-    mi::ssm::ssm_scan_kernel<0><<<grid, mi::ssm::SCAN_THREADS, 0, (cudaStream_t)stream>>>(act, bc, ldbc, src, z, ldz,
-                                                                                          base, y, amax, L, D);
+    mi::ssm::launch_scan<0>(mi::ssm::pick_split(batch, D), batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax,
+                            (cudaStream_t)stream);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
 
 extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const int8_t* dtq, int ldq, const float* dts,
                               const int8_t* w_dt, const float* w_dt_scale, int R, const float* z, int ldz,
-                              const float* base, float* y, float* amax, int batch, int L, int D, int N, void* stream) {
+                              const float* base, float* y, float* amax, int batch, int L, int D, int N, int split,
+                              void* stream) {
     if (!act || !bc || !dtq || !dts || !w_dt || !w_dt_scale || !z || !base || !y) return MI_ERR_INVALID;
     if (N != mi::ssm::NS) return MI_ERR_UNSUPPORTED;
     if (batch <= 0 || L <= 0 || D <= 0 || R <= 0 || ldbc < 2 * N || ldz < D) return MI_ERR_INVALID;
+    if (split != 0 && split != 1 && split != 2 && split != 4) return MI_ERR_INVALID;
     const int R16 = (R + 15) / 16 * 16;
     if (R16 > 4 * mi::ssm::MAX_RW || ldq < R16 || (ldq & 15)) return MI_ERR_UNSUPPORTED;
     if (batch > 65535) return MI_ERR_UNSUPPORTED;
@@ -435,28 +707,15 @@ extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const
         return MI_ERR_UNSUPPORTED;
     if (((uintptr_t)dts) & 3) return MI_ERR_UNSUPPORTED;
     if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
-    dim3 grid(mi::cdiv(D, mi::ssm::SCAN_THREADS), batch);
+    if (split == 0) split = mi::ssm::pick_split(batch, D);
     mi::ssm::DtSource src{nullptr, dtq, ldq, dts, w_dt, w_dt_scale};
     cudaStream_t s = (cudaStream_t)stream;
     switch (R16 / 4) {
-        case 4:
-            mi::ssm::ssm_scan_kernel<4><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
-                                                                                amax, L, D);
-            break;
-        case 8:
-            mi::ssm::ssm_scan_kernel<8><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
-                                                                                amax, L, D);
-            break;
-        case 12:
-            mi::ssm::ssm_scan_kernel<12><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
-                                                                                 amax, L, D);
-            break;
-        case 16:
-            mi::ssm::ssm_scan_kernel<16><<<grid, mi::ssm::SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y,
-                                                                                 amax, L, D);
-            break;
-        default:
-            return MI_ERR_UNSUPPORTED;
+        case 4: mi::ssm::launch_scan<4>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
+        case 8: mi::ssm::launch_scan<8>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
+        case 12: mi::ssm::launch_scan<12>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
+        case 16: mi::ssm::launch_scan<16>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
+        default: return MI_ERR_UNSUPPORTED;
     }
     MI_CHECK_LAUNCH();
     return MI_OK;

@@ -82,7 +82,8 @@ def launches_per_forward(n_layer: int) -> int:
     return 2 + 9 * n_layer
 
 
-def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N: int, timer=NO_TIMER):
+def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N: int, timer=NO_TIMER,
+              scan_split: int = 0):
     """Everything between the in_proj output (ws.xz) and the out_proj output (ws.out)."""
     with timer("conv_act_quant"):
         kernels.conv_act_quant(ws.xz, p["conv_w"], p["conv_b"], batch, L, di, act=ws.act, xq=ws.xq_i,
@@ -95,7 +96,7 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
         # dt_proj is fused into the scan (each channel's dot product by dp4a)
         ws.amax.zero_()
         kernels.ssm_scan_dt(ws.act, ws.xp[:, R:], ws.dtq, ws.dts, p["w_dt"][0], p["w_dt"][1], R, ws.xz[:, di:],
-                            p["base"], batch, L, y=ws.y, amax=ws.amax)
+                            p["base"], batch, L, y=ws.y, amax=ws.amax, split=scan_split)
     with timer("quant_y"):
         kernels.quantize_rows(ws.y, out=ws.xq_i, xscale=ws.xs_i, amax=ws.amax)
     with timer("gemm_out_proj"):
@@ -127,6 +128,8 @@ class PrefillEngine:
         self.out_scale = torch.tensor([model.output_scale], dtype=torch.float32, device=dev)
         self._versions = self._version_key(model)
         self._ws: Dict[Tuple[int, int], _Workspace] = {}
+        # lanes per channel of the fused scan (0: chosen per launch from batch x channels)
+        self.scan_split = 0
 
     @staticmethod
     def _version_key(model):
@@ -159,7 +162,7 @@ class PrefillEngine:
         for i, p in enumerate(self.layers):
             with timer("gemm_in_proj"):
                 kernels.bitlinear_i8(ws.xq_d, p["w_in"][0], ws.xs_d, p["w_in"][1], out=ws.xz)
-            _ssm_half(p, ws, batch, L, d, di, R, N, timer)
+            _ssm_half(p, ws, batch, L, d, di, R, N, timer, self.scan_split)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
             g, s = (nxt["gamma"], nxt["step"]) if nxt else (self.gamma_f, self.step_f)
             with timer("rowprep"):

@@ -190,9 +190,11 @@ def ssm_scan(act, bc, modraw, z, base, batch: int, L: int, y=None, amax=None):
     return y
 
 
-def ssm_scan_dt(act, bc, dtq, dts, w_dt, w_dt_scale, R: int, z, base, batch: int, L: int, y=None, amax=None):
+def ssm_scan_dt(act, bc, dtq, dts, w_dt, w_dt_scale, R: int, z, base, batch: int, L: int, y=None, amax=None,
+                split: int = 0):
     """ssm_scan with dt_proj fused (see mi_ssm_scan_dt): dtq int8 [T, ldq] quantised
-    dt rows, dts [T] their scales, w_dt int8 [D, ceil16(R)], w_dt_scale [1]."""
+    dt rows, dts [T] their scales, w_dt int8 [D, ceil16(R)], w_dt_scale [1].
+    split: lanes per channel (0 = automatic)."""
     D, N = base.shape
     T = batch * L
     if y is None:
@@ -200,7 +202,7 @@ def ssm_scan_dt(act, bc, dtq, dts, w_dt, w_dt_scale, R: int, z, base, batch: int
     _lib.check(_lib.load().mi_ssm_scan_dt(act.data_ptr(), bc.data_ptr(), bc.stride(0), dtq.data_ptr(), dtq.stride(0),
                                           dts.data_ptr(), w_dt.data_ptr(), w_dt_scale.data_ptr(), R, z.data_ptr(),
                                           z.stride(0), base.data_ptr(), y.data_ptr(), _ptr(amax), batch, L, D, N,
-                                          _stream()), "mi_ssm_scan_dt")
+                                          int(split), _stream()), "mi_ssm_scan_dt")
     return y
 
 

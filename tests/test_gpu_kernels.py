@@ -215,8 +215,9 @@ def test_ssm_scan_matches_oracle(cuda_dev, bsz, L, D, R):
     _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
 
 
-@pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (2, 9, 96, 64), (1, 33, 64, 20)])
-def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R):
+@pytest.mark.parametrize("split", [1, 2, 4, 0])
+@pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (2, 9, 96, 64), (1, 33, 72, 20)])
+def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split):
     """dt_proj fused into the scan: same result as quantise -> BitLinear -> scan."""
     k = _mi()
     g = torch.Generator().manual_seed(5 * bsz + L + D + R)
@@ -241,7 +242,7 @@ def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R):
     w16[:, :R] = wdt
     amax = torch.zeros(T, device=cuda_dev)
     y = k.ssm_scan_dt(dv(act), xpd[:, R:], dtq_d, dts_d, dv(w16), dv(torch.tensor([ws])), R, zd[:, D:], dv(base),
-                      bsz, L, amax=amax)
+                      bsz, L, amax=amax, split=split)
     _eq(y, y_ref, "fused-dt ssm y")
     _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
 
