@@ -129,6 +129,20 @@ int mi_conv_act_quant(const float* xz, int ldx, const float* w, const float* bia
                       int8_t* xq, float* xscale, float* amax_ws, int batch, int L, int D, void* stream);
 
 /*
+ * mi_conv_act_quant without the caller-provided workspace, for hosts that
+ * cannot call cudaMalloc (a runtime whose device memory belongs to another
+ * allocator, a serving loop that must not allocate).  No counterpart in the
+ * reference.  The row-absmax scratch is a fixed array inside the library:
+ * batch * L <= 262144 rows, larger requests return MI_ERR_UNSUPPORTED.  The
+ * first call on a device looks the array's device address up (make that first
+ * call before any stream capture).  Every call shares the array: calls that
+ * overlap on the GPU race with each other; each call zero-fills the rows it
+ * uses before using them.  Allocates nothing.
+ */
+int mi_conv_act_quant_noalloc(const float* xz, int ldx, const float* w, const float* bias, float* act,
+                              int8_t* xq, float* xscale, int batch, int L, int D, void* stream);
+
+/*
  * Selective-scan section of MambaIntegerBlock from the dt_proj output on:
  * decay clamp, dt, u = (x*dt)*B, convex dyadic scan h = h*d + (1-d)*u with
  * d = n/2^15, y = sum_n h*C (FMA, n ascending), gate y*sigmoid_alg(z).

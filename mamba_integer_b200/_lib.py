@@ -34,6 +34,7 @@ SIGNATURES = {
     "mi_rowprep": [_p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mi_bitlinear_i8": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
+    "mi_conv_act_quant_noalloc": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_ssm_scan": [_p, _p, _i, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
     "mi_ssm_scan_dt": [_p, _p, _i, _p, _i, _p, _p, _p, _i, _p, _i, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_scan_convex": [_p, _p, _p, _i, _i, _i, _p],

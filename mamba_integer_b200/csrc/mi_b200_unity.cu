@@ -6,3 +6,4 @@
 #include "rowops.cu"
 #include "ssm.cu"
 #include "gemm_i8.cu"
+#include "noalloc.cu"
