@@ -116,6 +116,33 @@ int mi_bitlinear_i8(const int8_t* A, int lda, const int8_t* W, const float* a_sc
                     int K, int epilogue, void* stream);
 
 /*
+ * 2-bit packed ternary weights.  Wp [N, K/4] bytes, row-major; each
+ * little-endian 32-bit word holds 16 consecutive weights k = 16g .. 16g+15,
+ * weight 16g + 4q + j in bits [p, p + 2), p = 4j + 2(q & 1) + 16(q >> 1), as a
+ * 2-bit two's complement value (00 = 0, 01 = +1, 11 = -1).
+ * mi_pack_ternary: W int8 [N, K] (row stride ldw) -> Wp; K % 16 == 0,
+ * ldw % 16 == 0; a value outside {-1, 0, 1} is stored as 0 and sets
+ * MI_DEV_PRECOND.
+ * Replaces the ternarisation result of weight_quant_ternary,
+ * src/rational_bitnet.py:63-85 (kept as fp32 {-1,0,1} by the reference and
+ * as int8 by scripts/export_int8.py:77-81): the packed form is this library's
+ * storage format.
+ */
+int mi_pack_ternary(const int8_t* W, int ldw, uint8_t* Wp, int N, int K, void* stream);
+
+/*
+ * mi_bitlinear_i8 with 2-bit packed weights: the TMA loads packed K-slices,
+ * the kernel expands them to int8 in shared memory and feeds the same
+ * tcgen05 kind::i8 MMAs; results are identical to mi_bitlinear_i8 on the
+ * unpacked weights.  K % 64 == 0 (packed rows of K/4 bytes, 16-byte pitch).
+ * Replaces: launch_bitlinear, src/cuda_kernels/bitlinear.cu:74-90, and the
+ * matmul + rescale of BitLinear.forward, src/rational_bitnet.py:204-208.
+ */
+int mi_bitlinear_packed(const int8_t* A, int lda, const uint8_t* Wp, const float* a_scale,
+                        const float* w_scale, const float* out_scale, void* out, int ldo, int M,
+                        int N, int K, int epilogue, void* stream);
+
+/*
  * Causal depthwise conv (4 taps, bias first then one FMA per tap) +
  * ste_clamp(-50, 50) + squareplus (3 Newton steps), then int8 quantisation of
  * each row of the activation.

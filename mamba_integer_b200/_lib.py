@@ -33,6 +33,8 @@ SIGNATURES = {
     "mi_quantize_rows": [_p, _i, _i, _i, _p, _i, _p, _p, _p],
     "mi_rowprep": [_p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mi_bitlinear_i8": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
+    "mi_pack_ternary": [_p, _i, _p, _i, _i, _p],
+    "mi_bitlinear_packed": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_conv_act_quant_noalloc": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_ssm_scan": [_p, _p, _i, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],

@@ -14,7 +14,11 @@
 //                    thread), dequantise acc * (w_scale * a_scale[m])
 //                    [* out_scale] exactly as BitLinear.forward does
 //                    (src/rational_bitnet.py:204-208), stage 32x32 boxes in
-//                    swizzled shared memory, TMA bulk tensor store.
+//                    swizzled shared memory, TMA bulk tensor store;
+//   warps 6-13       (2-bit packed weights only) unpack: the TMA brings the
+//                    K-slice of packed weights (BN rows x 32 bytes); these
+//                    warps expand it to int8 in the 128-byte-swizzled layout
+//                    the MMA reads, then release the stage to the MMA issuer.
 // Every mbarrier wait is bounded (about 2 s of clock); on expiry the CTA sets
 // MI_DEV_TIMEOUT, stops issuing, frees its tensor memory and exits.
 //
@@ -30,22 +34,39 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes (= int8 elements) of K per stage: one 128-byte swizzle row
+constexpr int BKP = BK / 4;  // bytes of one packed K-slice row (4 ternary weights per byte)
 constexpr int EPI_WARPS = 4;
+constexpr int UNPACK_WARPS = 8;
 constexpr int THREADS = 64 + 32 * EPI_WARPS;  // producer warp, MMA warp, 4 epilogue warps
+constexpr int THREADS_PACKED = THREADS + 32 * UNPACK_WARPS;  // + 8 unpack warps
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 
-template <int BN>
+template <bool PACKED>
+constexpr int threads_of() { return PACKED ? THREADS_PACKED : THREADS; }
+
+template <int BN, bool PACKED = false>
 struct Cfg {
-    static constexpr int STAGES = 4;
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int P_LOAD = PACKED ? BN * BKP : 0;             // packed bytes the TMA brings per stage
+    static constexpr int P_BYTES = (P_LOAD + 1023) / 1024 * 1024;    // their slot, padded to the 1 KB pitch
+    // Load ring: each stage holds the A slice and the weight slice (int8, or
+    // packed).  Packed weights are expanded into a separate, shorter ring of
+    // int8 tiles, so the load ring (small packed slices) can run deeper and
+    // cover the load latency plus the unpack.  256-wide tiles read each A
+    // slice once per 256 output columns.
+    static constexpr int STAGES = PACKED ? (BN > 128 ? 5 : 6) : 4;
+    static constexpr int STAGE_BYTES = A_BYTES + (PACKED ? P_BYTES : B_BYTES);
+    static constexpr int BSTAGES = PACKED ? (BN > 128 ? 2 : 3) : 0;  // int8 weight tiles (packed only)
+    static constexpr int BSM = BSTAGES > 0 ? BSTAGES : 1;           // modulus for the ring index
     static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per accumulator
     static constexpr int EPI_BOXES = (BN + 31) / 32;   // 32-column output boxes per tile
-    static constexpr int STG_BUFS = 4;                              // staging boxes per epilogue warp
+    static constexpr int STG_BUFS = (PACKED || BN > 128) ? 2 : 4;  // staging boxes per epilogue warp
     static constexpr int STG_BYTES = EPI_WARPS * STG_BUFS * 4096;  // (bulk stores kept in flight)
     static constexpr int BAR_BYTES = 256;
-    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BSTAGES * B_BYTES + STG_BYTES + BAR_BYTES;
+    static_assert(B_BYTES % 1024 == 0, "int8 weight tiles keep the 1 KB alignment");
+    static_assert(8 * (2 * STAGES + 4 + 2 * BSTAGES) + 8 <= BAR_BYTES, "barrier block");
     static_assert(STAGE_BYTES % 1024 == 0, "stage must keep 1024-byte alignment for the 128B swizzle");
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "UMMA N for M=128");
     static_assert(2 * TMEM_COLS <= 512, "two accumulators must fit in TMEM");
@@ -144,30 +165,87 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// 2-bit packed ternary weights.  Row n of the packed matrix holds K/4 bytes;
+// each little-endian 32-bit word covers 16 consecutive weights k = 16g .. 16g+15,
+// weight 16g + 4q + j in bits [p, p + 2), p = 4j + 2(q & 1) + 16(q >> 1), as a
+// 2-bit two's complement value (00 = 0, 01 = +1, 11 = -1).  The layout puts
+// the four codes of output word q in the low bits of the four nibbles of
+// (w >> (2(q & 1) + 16(q >> 1))) & 0x3333, a byte-permute selector: one
+// shift, one mask and one PRMT from the table {0, +1, 0, -1} per 4 weights.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t prmt_table(uint32_t sel) {
+    uint32_t r;
+    // source bytes 0..3 = 0x00, 0x01, 0x00, 0xFF (code 2 is never written)
+    asm("prmt.b32 %0, %1, %1, %2;" : "=r"(r) : "r"(0xFF000100u), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ uint4 unpack16(uint32_t w) {
+    return make_uint4(prmt_table(w & 0x3333u), prmt_table((w >> 2) & 0x3333u), prmt_table((w >> 16) & 0x3333u),
+                      prmt_table((w >> 18) & 0x3333u));
+}
+
+// Expand one stage's packed K-slice (ROWS x 32 bytes, dense) into the int8
+// tile (ROWS x 128 bytes, 128-byte swizzle: 16-byte chunk c of row r at
+// c ^ (r & 7); the tile is 1024-byte aligned).  Each unpack thread takes
+// 16-byte quads of packed bytes (4 words = 4 output chunks of one row), all
+// loads issued before the stores; `tid` counts the unpack threads.
+template <int ROWS>
+__device__ __forceinline__ void unpack_slice(const unsigned char* packed, unsigned char* tile, int tid) {
+    constexpr int QUADS = ROWS * 2;  // a packed row is 2 quads
+    constexpr int NT = 32 * UNPACK_WARPS;
+    constexpr int ITERS = (QUADS + NT - 1) / NT;
+    uint4 v[ITERS];
+#pragma unroll
+    for (int i = 0; i < ITERS; i++) {
+        const int qd = tid + i * NT;
+        if (qd < QUADS) v[i] = reinterpret_cast<const uint4*>(packed)[qd];
+    }
+#pragma unroll
+    for (int i = 0; i < ITERS; i++) {
+        const int qd = tid + i * NT;
+        if (qd < QUADS) {
+            const int r = qd >> 1, c0 = (qd & 1) * 4, sw = r & 7;
+            unsigned char* row = tile + r * 128;
+            *reinterpret_cast<uint4*>(row + (((c0 + 0) ^ sw) << 4)) = unpack16(v[i].x);
+            *reinterpret_cast<uint4*>(row + (((c0 + 1) ^ sw) << 4)) = unpack16(v[i].y);
+            *reinterpret_cast<uint4*>(row + (((c0 + 2) ^ sw) << 4)) = unpack16(v[i].z);
+            *reinterpret_cast<uint4*>(row + (((c0 + 3) ^ sw) << 4)) = unpack16(v[i].w);
+        }
+    }
+    // the MMA reads the tile through the async proxy
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+
 // Persistent kernel: each CTA walks the output tiles blockIdx.x,
 // blockIdx.x + gridDim.x, ... (N fastest, so CTAs working at the same time
 // share the A row-block in L2).  The smem ring and the two TMEM accumulators
 // carry across tiles, so the epilogue of tile i overlaps the mainloop of
 // tile i+1.
-template <int BN>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int BN, bool PACKED>
+__global__ void __launch_bounds__(threads_of<PACKED>(), 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
                const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K, int epi) {
-    using C = Cfg<BN>;
+    using C = Cfg<BN, PACKED>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-aligned tiles
     unsigned char* gbase = smem_raw + (base - raw);
-    const uint32_t stg_base = base + C::STAGES * C::STAGE_BYTES;  // epilogue staging (1024-aligned)
+    const uint32_t wring = base + C::STAGES * C::STAGE_BYTES;       // int8 weight tiles (packed only)
+    const uint32_t stg_base = wring + C::BSTAGES * C::B_BYTES;      // epilogue staging (1024-aligned)
     const uint32_t bars = stg_base + C::STG_BYTES;
-    // barriers: full[S], empty[S], tfull[2], tempty[2]; then the TMEM slot and the abort flag
+    // barriers: full[S], empty[S], tfull[2], tempty[2], then (packed only)
+    // bready[BS] (int8 tile written) and bfree[BS] (its MMAs done); then the
+    // TMEM slot and the abort flag
     auto full_bar = [&](int s) { return bars + 8u * s; };
     auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
     auto tfull_bar = [&](int a) { return bars + 8u * (2 * C::STAGES + a); };
     auto tempty_bar = [&](int a) { return bars + 8u * (2 * C::STAGES + 2 + a); };
+    auto bready_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + 4 + b); };
+    auto bfree_bar = [&](int b) { return bars + 8u * (2 * C::STAGES + 4 + C::BSTAGES + b); };
     uint32_t* tmem_slot =
-        reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * C::STAGES + 4));
+        reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * C::STAGES + 4 + 2 * C::BSTAGES));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -184,6 +262,10 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
             mbar_init(tempty_bar(a), EPI_WARPS);
+        }
+        for (int b = 0; b < C::BSTAGES; b++) {
+            mbar_init(bready_bar(b), UNPACK_WARPS);
+            mbar_init(bfree_bar(b), 1);
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -210,9 +292,15 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     const int s = g % C::STAGES;
                     if (g >= C::STAGES && !mbar_wait(empty_bar(s), ((g / C::STAGES) - 1) & 1, abort_flag)) break;
                     const uint32_t sa = base + s * C::STAGE_BYTES;
-                    mbar_expect_tx(full_bar(s), C::STAGE_BYTES);
-                    tma_load_2d(sa, &tmA, full_bar(s), i * BK, m0);
-                    tma_load_2d(sa + C::A_BYTES, &tmB, full_bar(s), i * BK, n0);
+                    if (PACKED) {
+                        mbar_expect_tx(full_bar(s), C::A_BYTES + C::P_LOAD);
+                        tma_load_2d(sa, &tmA, full_bar(s), i * BK, m0);
+                        tma_load_2d(sa + C::A_BYTES, &tmB, full_bar(s), i * BKP, n0);
+                    } else {
+                        mbar_expect_tx(full_bar(s), C::A_BYTES + C::B_BYTES);
+                        tma_load_2d(sa, &tmA, full_bar(s), i * BK, m0);
+                        tma_load_2d(sa + C::A_BYTES, &tmB, full_bar(s), i * BK, n0);
+                    }
                 }
             }
             if (*abort_flag) {
@@ -238,22 +326,51 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                 bool ok = true;
                 for (int i = 0; i < num_k; i++, g++) {
                     const int s = g % C::STAGES;
-                    if (!mbar_wait(full_bar(s), (g / C::STAGES) & 1, abort_flag)) {
+                    const int b = g % C::BSM;
+                    if (!mbar_wait(full_bar(s), (g / C::STAGES) & 1, abort_flag) ||
+                        (PACKED && !mbar_wait(bready_bar(b), (g / C::BSM) & 1, abort_flag))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const uint32_t sa = base + s * C::STAGE_BYTES;
+                    const uint32_t sb = PACKED ? wring + b * C::B_BYTES : sa + C::A_BYTES;
 #pragma unroll
                     for (int kk = 0; kk < BK / 32; kk++) {
                         const uint64_t ad = sdesc_sw128(sa + kk * 32);
-                        const uint64_t bd = sdesc_sw128(sa + C::A_BYTES + kk * 32);
+                        const uint64_t bd = sdesc_sw128(sb + kk * 32);
                         mma_i8(tacc, ad, bd, idesc, (i | kk) != 0);
                     }
                     mma_commit(empty_bar(s));
+                    if (PACKED) mma_commit(bfree_bar(b));
                 }
                 if (!ok) break;
                 mma_commit(tfull_bar(a));
+            }
+        }
+    } else if (PACKED && warp >= 2 + EPI_WARPS) {
+        // ---------------- unpack (warps 6..13) ----------------
+        // Stage g: the packed slice of load slot g % STAGES is expanded into
+        // int8 tile g % BSTAGES once that tile's previous MMAs completed.  The
+        // load slot itself is released by the MMA commit (which follows this
+        // stage's bready), so the packed bytes stay put while they are read.
+        const int tid = threadIdx.x - 32 * (2 + EPI_WARPS);
+        int g = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            for (int i = 0; i < num_k; i++, g++) {
+                const int s = g % C::STAGES;
+                const int b = g % C::BSM;
+                const bool ready = mbar_wait(full_bar(s), (g / C::STAGES) & 1, abort_flag) &&
+                                   (g < C::BSTAGES || mbar_wait(bfree_bar(b), ((g / C::BSM) - 1) & 1, abort_flag));
+                if (!__all_sync(0xffffffffu, ready)) {
+                    ok = false;
+                    break;
+                }
+                unpack_slice<BN>(gbase + s * C::STAGE_BYTES + C::A_BYTES, gbase + (wring - base) + b * C::B_BYTES,
+                                 tid);
+                __syncwarp();
+                if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bready_bar(b)) : "memory");
             }
         }
     } else {
@@ -301,8 +418,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                 }
                 // the staging buffer used STG_BUFS stores ago must have been read
-                static_assert(C::STG_BUFS == 4, "wait_group.read count below");
-                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 3;\n" ::: "memory");
+                static_assert(C::STG_BUFS == 4 || C::STG_BUFS == 2, "power-of-two staging ring");
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(C::STG_BUFS - 1) : "memory");
                 __syncwarp();
                 unsigned char* rowp = stg_g + (nst & (C::STG_BUFS - 1)) * 4096 + lane * 128;
 #pragma unroll
@@ -342,16 +459,29 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // the persistent CTAs.
 // ---------------------------------------------------------------------------
 constexpr int ARES_MAXK = 6;    // K slices held (K <= 768)
-constexpr int ARES_SB = 6;      // weight ring depth
 constexpr int ARES_BN = 128;
 constexpr int ARES_STG = 2;     // staging boxes per epilogue warp
 constexpr int ARES_A_BYTES = ARES_MAXK * BM * BK;              // 96 KB
 constexpr int ARES_B_BYTES = ARES_BN * BK;                     // 16 KB per slice
+constexpr int ARES_P_BYTES = ARES_BN * BKP;                    // 4 KB per packed slice
 constexpr int ARES_STG_BYTES = EPI_WARPS * ARES_STG * 4096;    // 32 KB
-constexpr int ARES_SMEM = 1024 + ARES_A_BYTES + ARES_SB * ARES_B_BYTES + ARES_STG_BYTES + 256;
-static_assert(ARES_SMEM <= 227 * 1024, "shared memory per CTA");
 
-__global__ void __launch_bounds__(THREADS, 1)
+// Weight rings: 6 int8 slices loaded by the TMA; or, with packed weights, 8
+// packed slices in flight (TMA) feeding 3 int8 slices (written by the unpack
+// warps, read by the MMAs).
+template <bool PACKED>
+struct AresCfg {
+    static constexpr int SB = PACKED ? 3 : 6;
+    static constexpr int PSB = PACKED ? 8 : 0;
+    static constexpr int PSM = PSB > 0 ? PSB : 1;  // modulus for the packed ring index
+    static constexpr int SMEM = 1024 + ARES_A_BYTES + SB * ARES_B_BYTES + PSB * ARES_P_BYTES + ARES_STG_BYTES + 256;
+    static_assert(ARES_P_BYTES % 1024 == 0, "packed slices keep the 1 KB pitch");
+    static_assert(8 * (2 * SB + 6 + 2 * PSB) + 8 <= 256, "barrier block");
+    static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+};
+
+template <bool PACKED>
+__global__ void __launch_bounds__(threads_of<PACKED>(), 1)
 gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
                     const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K,
@@ -359,22 +489,32 @@ gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     constexpr int BN = ARES_BN;
     constexpr int TMEM_COLS = 128;
     constexpr int EPI_BOXES = BN / 32;
+    constexpr int ARES_SB = AresCfg<PACKED>::SB;
+    constexpr int PSB = AresCfg<PACKED>::PSB;
+    constexpr int PSM = AresCfg<PACKED>::PSM;
+    constexpr int SLOT = ARES_B_BYTES;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     unsigned char* gbase = smem_raw + (base - raw);
     const uint32_t a_base = base;                                   // ARES_MAXK x 16 KB
-    const uint32_t b_base = a_base + ARES_A_BYTES;                  // ARES_SB x 16 KB
-    const uint32_t stg_base = b_base + ARES_SB * ARES_B_BYTES;      // staging
+    const uint32_t b_base = a_base + ARES_A_BYTES;                  // ARES_SB int8 weight slices
+    const uint32_t p_base = b_base + ARES_SB * SLOT;                // PSB packed slices (packed only)
+    const uint32_t stg_base = p_base + PSB * ARES_P_BYTES;          // staging
     const uint32_t bars = stg_base + ARES_STG_BYTES;
-    // barriers: bfull[SB], bempty[SB], tfull[2], tempty[2], afull, aempty; then TMEM slot, abort flag
+    // barriers: bfull[SB] (int8 slice ready: TMA, or the unpack warps), bempty[SB]
+    // (its MMAs done), tfull[2], tempty[2], afull, aempty, then (packed only)
+    // pfull[PSB] (packed slice landed) and pempty[PSB] (unpacked); then TMEM
+    // slot, abort flag
     auto bfull_bar = [&](int s) { return bars + 8u * s; };
     auto bempty_bar = [&](int s) { return bars + 8u * (ARES_SB + s); };
     auto tfull_bar = [&](int a) { return bars + 8u * (2 * ARES_SB + a); };
     auto tempty_bar = [&](int a) { return bars + 8u * (2 * ARES_SB + 2 + a); };
     const uint32_t afull_bar = bars + 8u * (2 * ARES_SB + 4);
     const uint32_t aempty_bar = bars + 8u * (2 * ARES_SB + 5);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * ARES_SB + 6));
+    auto pfull_bar = [&](int s) { return bars + 8u * (2 * ARES_SB + 6 + s); };
+    auto pempty_bar = [&](int s) { return bars + 8u * (2 * ARES_SB + 6 + PSB + s); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * ARES_SB + 6 + 2 * PSB));
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -392,8 +532,12 @@ gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < ARES_SB; s++) {
-            mbar_init(bfull_bar(s), 1);
+            mbar_init(bfull_bar(s), PACKED ? UNPACK_WARPS : 1);
             mbar_init(bempty_bar(s), 1);
+        }
+        for (int s = 0; s < PSB; s++) {
+            mbar_init(pfull_bar(s), 1);
+            mbar_init(pempty_bar(s), UNPACK_WARPS);
         }
         for (int a = 0; a < 2; a++) {
             mbar_init(tfull_bar(a), 1);
@@ -428,21 +572,33 @@ gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 for (int k = 0; k < num_k; k++) tma_load_2d(a_base + k * BM * BK, &tmA, afull_bar, k * BK, m0);
                 for (int nt = nt0; nt < nt1 && ok; nt++) {
                     for (int k = 0; k < num_k; k++, g++) {
-                        const int s = g % ARES_SB;
-                        if (g >= ARES_SB && !mbar_wait(bempty_bar(s), ((g / ARES_SB) - 1) & 1, abort_flag)) {
-                            ok = false;
-                            break;
+                        if (PACKED) {
+                            const int s = g % PSM;
+                            if (g >= PSB && !mbar_wait(pempty_bar(s), ((g / PSM) - 1) & 1, abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_expect_tx(pfull_bar(s), (uint32_t)ARES_P_BYTES);
+                            tma_load_2d(p_base + s * ARES_P_BYTES, &tmB, pfull_bar(s), k * BKP, nt * BN);
+                        } else {
+                            const int s = g % ARES_SB;
+                            if (g >= ARES_SB && !mbar_wait(bempty_bar(s), ((g / ARES_SB) - 1) & 1, abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            mbar_expect_tx(bfull_bar(s), (uint32_t)ARES_B_BYTES);
+                            tma_load_2d(b_base + s * SLOT, &tmB, bfull_bar(s), k * BK, nt * BN);
                         }
-                        mbar_expect_tx(bfull_bar(s), (uint32_t)ARES_B_BYTES);
-                        tma_load_2d(b_base + s * ARES_B_BYTES, &tmB, bfull_bar(s), k * BK, nt * BN);
                     }
                 }
             }
             if (*abort_flag) {
                 // let issued loads land before the CTA exits (bounded)
-                for (int j = (g > ARES_SB ? g - ARES_SB : 0); j < g; j++) {
+                const int ring = PACKED ? PSB : ARES_SB;
+                for (int j = (g > ring ? g - ring : 0); j < g; j++) {
                     const long long t0 = clock64();
-                    while (!mbar_try(bfull_bar(j % ARES_SB), (j / ARES_SB) & 1) && clock64() - t0 < WAIT_CYCLES) {
+                    const uint32_t bar = PACKED ? pfull_bar(j % PSM) : bfull_bar(j % ARES_SB);
+                    while (!mbar_try(bar, (j / ring) & 1) && clock64() - t0 < WAIT_CYCLES) {
                     }
                 }
                 if (ua > 0) {
@@ -479,7 +635,7 @@ gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         }
                         tc_fence_after();
                         const uint32_t sa = a_base + k * BM * BK;
-                        const uint32_t sb = b_base + s * ARES_B_BYTES;
+                        const uint32_t sb = b_base + s * SLOT;
 #pragma unroll
                         for (int kk = 0; kk < BK / 32; kk++)
                             mma_i8(tacc, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc, (k | kk) != 0);
@@ -490,6 +646,34 @@ gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 }
                 if (!ok) break;
                 mma_commit(aempty_bar);  // the unit's MMAs have all read A once they complete
+            }
+        }
+    } else if (PACKED && warp >= 2 + EPI_WARPS) {
+        // ---------------- unpack (warps 6..13), as in gemm_i8_kernel ----------------
+        const int tid = threadIdx.x - 32 * (2 + EPI_WARPS);
+        int g = 0;
+        bool ok = true;
+        for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+            int m0, nt0, nt1;
+            unit_range(u, m0, nt0, nt1);
+            for (int nt = nt0; nt < nt1 && ok; nt++) {
+                for (int k = 0; k < num_k; k++, g++) {
+                    // packed slice g % PSB -> int8 slice g % SB (free once its MMAs completed)
+                    const int ps = g % PSM, s = g % ARES_SB;
+                    const bool ready = mbar_wait(pfull_bar(ps), (g / PSM) & 1, abort_flag) &&
+                                       (g < ARES_SB || mbar_wait(bempty_bar(s), ((g / ARES_SB) - 1) & 1, abort_flag));
+                    if (!__all_sync(0xffffffffu, ready)) {
+                        ok = false;
+                        break;
+                    }
+                    unpack_slice<BN>(gbase + (p_base - base) + ps * ARES_P_BYTES, gbase + (b_base - base) + s * SLOT,
+                                     tid);
+                    __syncwarp();
+                    if (lane == 0) {
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(pempty_bar(ps)) : "memory");
+                        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bfull_bar(s)) : "memory");
+                    }
+                }
             }
         }
     } else {
@@ -583,9 +767,10 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 // 2-D tensor [rows, cols] of `esize`-byte elements with row pitch ld_bytes;
-// box = box_cols x box_rows, 128-byte swizzle (box_cols * esize == 128).
+// box = box_cols x box_rows, 128-byte swizzle (box_cols * esize == 128) or,
+// with swizzle = false, a dense box (packed weight slices: 32-byte rows).
 static int make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, long long ld_bytes, int box_cols,
-                     int box_rows, int esize) {
+                     int box_rows, int esize, bool swizzle = true) {
     auto enc = get_encode();
     if (!enc) return MI_ERR_CUDA;
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
@@ -594,25 +779,35 @@ static int make_tmap(CUtensorMap* tm, const void* ptr, int rows, int cols, long 
     cuuint32_t estr[2] = {1, 1};
     CUtensorMapDataType dt = esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
     CUresult r = enc(tm, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MI_OK : MI_ERR_CUDA;
 }
 
-template <int BN>
-static int launch(const int8_t* A, int lda, const int8_t* W, const float* a_scale, const float* w_scale,
+// Weight tensor map: int8 rows of K bytes (128-byte swizzled K-slices) or
+// packed rows of K/4 bytes (dense 32-byte slices).
+template <bool PACKED>
+static int make_wmap(CUtensorMap* tm, const void* W, int N, int K, int box_rows) {
+    if (PACKED) return make_tmap(tm, W, N, K / 4, K / 4, BKP, box_rows, 1, false);
+    return make_tmap(tm, W, N, K, K, BK, box_rows, 1);
+}
+
+template <int BN, bool PACKED>
+static int launch(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
                   const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
     // a tile whose last 32-column box sticks out past BN would overwrite the next tile
     if ((BN % 32) != 0 && N > BN) return MI_ERR_UNSUPPORTED;
     CUtensorMap ta, tb, tc;
     int rc = make_tmap(&ta, A, M, K, lda, BK, BM, 1);
     if (rc) return rc;
-    rc = make_tmap(&tb, W, N, K, K, BK, BN, 1);
+    rc = make_wmap<PACKED>(&tb, W, N, K, BN);
     if (rc) return rc;
     rc = make_tmap(&tc, out, M, N, (long long)ldo * 4, 32, 32, 4);
     if (rc) return rc;
-    using C = Cfg<BN>;
-    if (cudaFuncSetAttribute(gemm_i8_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+    using C = Cfg<BN, PACKED>;
+    if (cudaFuncSetAttribute(gemm_i8_kernel<BN, PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
         return MI_ERR_CUDA;
     static int num_sms = 0;
     if (!num_sms) {
@@ -623,7 +818,8 @@ static int launch(const int8_t* A, int lda, const int8_t* W, const float* a_scal
     }
     const int tiles = cdiv(M, BM) * cdiv(N, BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_i8_kernel<BN><<<grid, THREADS, C::SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M, N, K, epi);
+    gemm_i8_kernel<BN, PACKED><<<grid, threads_of<PACKED>(), C::SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale,
+                                                                         M, N, K, epi);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
@@ -639,16 +835,18 @@ static int sm_count() {
     return num_sms;
 }
 
-static int launch_ares(const int8_t* A, int lda, const int8_t* W, const float* a_scale, const float* w_scale,
+template <bool PACKED>
+static int launch_ares(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
                        const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
     CUtensorMap ta, tb, tc;
     int rc = make_tmap(&ta, A, M, K, lda, BK, BM, 1);
     if (rc) return rc;
-    rc = make_tmap(&tb, W, N, K, K, BK, ARES_BN, 1);
+    rc = make_wmap<PACKED>(&tb, W, N, K, ARES_BN);
     if (rc) return rc;
     rc = make_tmap(&tc, out, M, N, (long long)ldo * 4, 32, 32, 4);
     if (rc) return rc;
-    if (cudaFuncSetAttribute(gemm_i8_ares_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ARES_SMEM) !=
+    constexpr int SMEM = AresCfg<PACKED>::SMEM;
+    if (cudaFuncSetAttribute(gemm_i8_ares_kernel<PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) !=
         cudaSuccess)
         return MI_ERR_CUDA;
     const int sms = sm_count();
@@ -659,38 +857,90 @@ static int launch_ares(const int8_t* A, int lda, const int8_t* W, const float* a
     if (groups > tiles_n) groups = tiles_n;
     const int units = tiles_m * groups;
     const int grid = units < sms ? units : sms;
-    gemm_i8_ares_kernel<<<grid, THREADS, ARES_SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M, N, K, epi,
-                                                         groups);
+    gemm_i8_ares_kernel<PACKED><<<grid, threads_of<PACKED>(), SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M,
+                                                                        N, K, epi, groups);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
 
-}  // namespace gemm
-}  // namespace mi
-
-extern "C" int mi_bitlinear_i8(const int8_t* A, int lda, const int8_t* W, const float* a_scale, const float* w_scale,
-                               const float* out_scale, void* out, int ldo, int M, int N, int K, int epilogue,
-                               void* stream) {
-    using namespace mi::gemm;
+// Shape checks shared by both weight formats, then the kernel choice.
+template <bool PACKED>
+static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
+                     const float* out_scale, void* out, int ldo, int M, int N, int K, int epilogue, void* stream) {
     if (!A || !W || !out) return MI_ERR_INVALID;
     if (M <= 0 || N <= 0 || K <= 0) return MI_ERR_INVALID;
     if (epilogue != MI_EPI_I32 && epilogue != MI_EPI_F32_SCALED) return MI_ERR_INVALID;
     if (epilogue == MI_EPI_F32_SCALED && (!a_scale || !w_scale)) return MI_ERR_INVALID;
     if (K % 16 != 0 || lda < K || lda % 16 != 0 || N % 16 != 0) return MI_ERR_UNSUPPORTED;
+    if (PACKED && K % 64 != 0) return MI_ERR_UNSUPPORTED;  // packed rows of K/4 bytes: 16-byte pitch for the TMA
     if (ldo < N || ldo % 4 != 0) return MI_ERR_INVALID;
     if ((((uintptr_t)A) | ((uintptr_t)W)) & 15) return MI_ERR_INVALID;
     if (((uintptr_t)out) & 15) return MI_ERR_INVALID;
     if (K > 132104) return MI_ERR_UNSUPPORTED;
     cudaStream_t s = (cudaStream_t)stream;
     if (K <= ARES_MAXK * BK && N > 128)  // wide outputs over a short K: keep A resident
-        return launch_ares(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+        return launch_ares<PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (N <= 128 && N % 16 == 0 && N != 128) {
         // narrow projections (x_proj: N = dt_rank + 2*d_state) in one N tile
-        if (N <= 32) return launch<32>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
-        if (N <= 64) return launch<64>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
-        if (N <= 80) return launch<80>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
-        if (N <= 96) return launch<96>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
-        return launch<128>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+        if (N <= 32) return launch<32, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+        if (N <= 64) return launch<64, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+        if (N <= 80) return launch<80, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+        if (N <= 96) return launch<96, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+        return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     }
-    return launch<128>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+    if (N % 256 == 0)
+        return launch<256, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+    return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+}
+
+// Dense int8 ternary rows -> the 2-bit format (one thread per 16-weight word).
+// A value outside {-1, 0, 1} is stored as 0 and sets MI_DEV_PRECOND.
+__global__ void pack_ternary_kernel(const int8_t* __restrict__ W, int ldw, uint32_t* __restrict__ Wp, int N,
+                                    int K) {
+    const int words = K / 16;
+    const long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (i >= (long long)N * words) return;
+    const int n = (int)(i / words), g = (int)(i % words);
+    const int4 v = *reinterpret_cast<const int4*>(W + (size_t)n * ldw + 16 * g);
+    const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+    uint32_t w = 0;
+    bool bad = false;
+#pragma unroll
+    for (int e = 0; e < 16; e++) {
+        const int x = b[e];
+        bad |= (x < -1 || x > 1);
+        const uint32_t code = (x >= -1 && x <= 1) ? ((uint32_t)x & 3u) : 0u;
+        const int q = e >> 2, j = e & 3;  // weight 4q + j of the group
+        w |= code << (4 * j + 2 * (q & 1) + 16 * (q >> 1));
+    }
+    if (bad) raise_dev_error(MI_DEV_PRECOND);
+    Wp[i] = w;
+}
+
+}  // namespace gemm
+}  // namespace mi
+
+extern "C" int mi_pack_ternary(const int8_t* W, int ldw, uint8_t* Wp, int N, int K, void* stream) {
+    using namespace mi::gemm;
+    if (!W || !Wp || N <= 0 || K <= 0 || ldw < K) return MI_ERR_INVALID;
+    if (K % 16 != 0 || ldw % 16 != 0) return MI_ERR_UNSUPPORTED;
+    if ((((uintptr_t)W) & 15) || (((uintptr_t)Wp) & 3)) return MI_ERR_INVALID;
+    const long long words = (long long)N * (K / 16);
+    const int threads = 256;
+    pack_ternary_kernel<<<(unsigned)((words + threads - 1) / threads), threads, 0, (cudaStream_t)stream>>>(
+        W, ldw, reinterpret_cast<uint32_t*>(Wp), N, K);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+extern "C" int mi_bitlinear_packed(const int8_t* A, int lda, const uint8_t* Wp, const float* a_scale,
+                                   const float* w_scale, const float* out_scale, void* out, int ldo, int M, int N,
+                                   int K, int epilogue, void* stream) {
+    return mi::gemm::bitlinear<true>(A, lda, Wp, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, stream);
+}
+
+extern "C" int mi_bitlinear_i8(const int8_t* A, int lda, const int8_t* W, const float* a_scale, const float* w_scale,
+                               const float* out_scale, void* out, int ldo, int M, int N, int K, int epilogue,
+                               void* stream) {
+    return mi::gemm::bitlinear<false>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, stream);
 }

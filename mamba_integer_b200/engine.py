@@ -8,11 +8,12 @@ Per layer (T = batch*seq_len tokens, d = d_model, di = 2*d_model):
     conv_act     conv + ste_clamp + squareplus + int8 quant            [T, di]
     x_proj       tcgen05 GEMM  [T, di] x [R+2N, di]^T -> dt | B | C    [T, R+2N]
     dt quant     int8 quant of the dt columns                          [T, R]
-    dt_proj      tcgen05 GEMM  [T, R]  x [di, R]^T  -> decay_mod raw    [T, di]
-    ssm_scan     decay / dt / u / convex scan / h.C / gate             [T, di]
+    ssm_scan     dt_proj (int8 dot products by dp4a) / decay / dt / u /
+                 convex scan / h.C / gate                              [T, di]
     y quant      int8 quant                                            [T, di]
     out_proj     tcgen05 GEMM  [T, di] x [d, di]^T  -> out              [T, d]
 then norm_f + lm_head (GEMM with the output_scale in its epilogue).
+The GEMMs read the weights packed 2 bits each (mi_bitlinear_packed).
 The residual add of each block is folded into the next row pre-pass.
 """
 from __future__ import annotations
@@ -22,6 +23,7 @@ from typing import Dict, Tuple
 import torch
 
 from . import kernels
+from .rational_bitnet import ternary_matmul
 
 
 def _pad16(k: int) -> int:
@@ -52,8 +54,8 @@ def _layer_params(blk, dev):
     f = lambda t: t.detach().to(device=dev, dtype=torch.float32).contiguous()  # noqa: E731
     return dict(
         gamma=f(blk.norm.gamma), step=f(blk.norm.step_size).reshape(1),
-        w_in=blk.in_proj.packed(dev), w_x=blk.x_proj.packed(dev), w_dt=blk.dt_proj.packed(dev),
-        w_out=blk.out_proj.packed(dev),
+        w_in=blk.in_proj.device_weights(dev), w_x=blk.x_proj.device_weights(dev),
+        w_dt=blk.dt_proj.device_weights(dev), w_out=blk.out_proj.device_weights(dev),
         conv_w=f(blk.conv1d.weight).reshape(di, 4).contiguous(), conv_b=f(blk.conv1d.bias),
         base=f(blk.base_decay_nums), res_gate=f(blk.res_gate).reshape(1),
     )
@@ -89,22 +91,22 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
         kernels.conv_act_quant(ws.xz, p["conv_w"], p["conv_b"], batch, L, di, act=ws.act, xq=ws.xq_i,
                                xscale=ws.xs_i, amax_ws=ws.amax)
     with timer("gemm_x_proj"):
-        kernels.bitlinear_i8(ws.xq_i, p["w_x"][0], ws.xs_i, p["w_x"][1], out=ws.xp)
+        ternary_matmul(ws.xq_i, p["w_x"], ws.xs_i, out=ws.xp)
     with timer("quant_dt"):
         kernels.quantize_rows(ws.xp, K=R, out=ws.dtq, xscale=ws.dts)
     with timer("ssm_scan"):
         # dt_proj is fused into the scan (each channel's dot product by dp4a)
         ws.amax.zero_()
-        kernels.ssm_scan_dt(ws.act, ws.xp[:, R:], ws.dtq, ws.dts, p["w_dt"][0], p["w_dt"][1], R, ws.xz[:, di:],
+        kernels.ssm_scan_dt(ws.act, ws.xp[:, R:], ws.dtq, ws.dts, p["w_dt"].w8, p["w_dt"].scale, R, ws.xz[:, di:],
                             p["base"], batch, L, y=ws.y, amax=ws.amax, split=scan_split)
     with timer("quant_y"):
         kernels.quantize_rows(ws.y, out=ws.xq_i, xscale=ws.xs_i, amax=ws.amax)
     with timer("gemm_out_proj"):
-        kernels.bitlinear_i8(ws.xq_i, p["w_out"][0], ws.xs_i, p["w_out"][1], out=ws.out)
+        ternary_matmul(ws.xq_i, p["w_out"], ws.xs_i, out=ws.out)
 
 
 class PrefillEngine:
-    """Holds device copies of the packed weights and the per-shape workspaces."""
+    """Holds device copies of the quantised weights (2-bit packed) and the per-shape workspaces."""
 
     def __init__(self, model):
         cfg = model.config
@@ -124,7 +126,7 @@ class PrefillEngine:
         self.emb = f(model.embedding.weight)
         self.gamma_f = f(model.norm_f.gamma)
         self.step_f = f(model.norm_f.step_size).reshape(1)
-        self.w_lm = model.lm_head.packed(dev)
+        self.w_lm = model.lm_head.device_weights(dev)
         self.out_scale = torch.tensor([model.output_scale], dtype=torch.float32, device=dev)
         self._versions = self._version_key(model)
         self._ws: Dict[Tuple[int, int], _Workspace] = {}
@@ -161,7 +163,7 @@ class PrefillEngine:
             kernels.rowprep(g0, s0, T, d, ids=ids, emb=self.emb, x_out=ws.x, xq=ws.xq_d, xscale=ws.xs_d)
         for i, p in enumerate(self.layers):
             with timer("gemm_in_proj"):
-                kernels.bitlinear_i8(ws.xq_d, p["w_in"][0], ws.xs_d, p["w_in"][1], out=ws.xz)
+                ternary_matmul(ws.xq_d, p["w_in"], ws.xs_d, out=ws.xz)
             _ssm_half(p, ws, batch, L, d, di, R, N, timer, self.scan_split)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
             g, s = (nxt["gamma"], nxt["step"]) if nxt else (self.gamma_f, self.step_f)
@@ -171,8 +173,7 @@ class PrefillEngine:
         if logits is None:
             logits = torch.empty(T, V, dtype=torch.float32, device=self.dev)
         with timer("gemm_lm_head"):
-            kernels.bitlinear_i8(ws.xq_d, self.w_lm[0], ws.xs_d, self.w_lm[1], out_scale=self.out_scale,
-                                 out=logits.view(T, V))
+            ternary_matmul(ws.xq_d, self.w_lm, ws.xs_d, out_scale=self.out_scale, out=logits.view(T, V))
         return logits.view(batch, L, V)
 
 
@@ -190,7 +191,7 @@ def run_block(blk, hidden_states: torch.Tensor) -> torch.Tensor:
     ws = _Workspace(batch * L, d, di, R, N, dev)
     x = hidden_states.detach().float().contiguous().view(batch * L, d)
     kernels.rowprep(p["gamma"], p["step"], batch * L, d, x=x, xq=ws.xq_d, xscale=ws.xs_d)
-    kernels.bitlinear_i8(ws.xq_d, p["w_in"][0], ws.xs_d, p["w_in"][1], out=ws.xz)
+    ternary_matmul(ws.xq_d, p["w_in"], ws.xs_d, out=ws.xz)
     _ssm_half(p, ws, batch, L, d, di, R, N)
     out = torch.empty_like(x)
     kernels.rowprep(p["gamma"], p["step"], batch * L, d, x=x, delta=ws.out, res_gate=p["res_gate"], x_out=out)

@@ -151,6 +151,39 @@ def bitlinear_i8(A: torch.Tensor, W: torch.Tensor, a_scale: Optional[torch.Tenso
     return out
 
 
+def pack_ternary(W: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """int8 ternary weights [N, K] -> 2-bit packed [N, K/4] uint8 (on the GPU)."""
+    _need(W, torch.int8, "W")
+    N, K = W.shape
+    if out is None:
+        out = torch.empty(N, K // 4, dtype=torch.uint8, device=W.device)
+    _lib.check(_lib.load().mi_pack_ternary(W.data_ptr(), W.stride(0), out.data_ptr(), N, K, _stream()),
+               "mi_pack_ternary")
+    return out
+
+
+def bitlinear_packed(A: torch.Tensor, Wp: torch.Tensor, a_scale: Optional[torch.Tensor] = None,
+                     w_scale: Optional[torch.Tensor] = None, out_scale: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None, K: Optional[int] = None) -> torch.Tensor:
+    """bitlinear_i8 with 2-bit packed weights Wp uint8 [N, K/4] (see pack_ternary)."""
+    _need(Wp, torch.uint8, "Wp")
+    if A.dim() != 2 or A.stride(1) != 1:
+        raise ValueError("A must be 2-D with unit column stride")
+    _need(A, torch.int8, "A", contiguous=False)
+    M = A.shape[0]
+    N = Wp.shape[0]
+    K = 4 * Wp.shape[1] if K is None else K
+    scaled = a_scale is not None
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32 if scaled else torch.int32, device=A.device)
+    epi = _lib.MI_EPI_F32_SCALED if scaled else _lib.MI_EPI_I32
+    _lib.check(_lib.load().mi_bitlinear_packed(A.data_ptr(), A.stride(0), Wp.data_ptr(), _ptr(a_scale),
+                                               _ptr(w_scale), _ptr(out_scale), out.data_ptr(), out.stride(0), M, N,
+                                               K, epi, _stream()),
+               "mi_bitlinear_packed")
+    return out
+
+
 # ---------------------------------------------------------------------------
 # conv / scan / element-wise
 # ---------------------------------------------------------------------------

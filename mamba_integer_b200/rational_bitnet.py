@@ -2,17 +2,20 @@
 
 Same constructor, parameter names and forward signature as the reference
 (src/rational_bitnet.py:114-219).  Differences by design:
-  * the ternary weights are quantised once and cached as int8 on the device
-    (re-quantised only when ``weight._version`` changes); the reference
-    re-quantises on every eval forward with identical results;
+  * the ternary weights are quantised once and cached on the device, as int8
+    and packed 2 bits per weight (re-quantised only when ``weight._version``
+    changes); the reference re-quantises on every eval forward with identical
+    results;
   * forward runs only on CUDA tensors: per-token int8 quantisation
     (mi_quantize_rows) then the tcgen05 int8 GEMM with the BitLinear rescale
-    in its epilogue (mi_bitlinear_i8).  There is no CPU path.
+    in its epilogue, fed from the 2-bit packed weights (mi_bitlinear_packed;
+    mi_bitlinear_i8 when the padded input width is not a multiple of 64).
+    There is no CPU path.
 """
 from __future__ import annotations
 
 import math
-from typing import Tuple
+from typing import NamedTuple, Optional, Tuple
 
 import torch
 import torch.nn as nn
@@ -48,6 +51,23 @@ def _pad16(k: int) -> int:
     return (k + 15) // 16 * 16
 
 
+class TernaryWeights(NamedTuple):
+    """Device copies of one BitLinear's quantised weights."""
+    w8: torch.Tensor            # int8 {-1,0,1} [out, in padded to 16]
+    w2: Optional[torch.Tensor]  # 2-bit packed uint8 [out, K/4] (None when the padded K is not a multiple of 64)
+    scale: torch.Tensor         # fp32 [1]: the AbsMean scale
+
+
+def ternary_matmul(xq: torch.Tensor, tw: TernaryWeights, xs: Optional[torch.Tensor], out=None, out_scale=None,
+                   K: Optional[int] = None) -> torch.Tensor:
+    """xq int8 [M, K] against the ternary weights, with the BitLinear rescale
+    acc * (w_scale * xs[m]) [* out_scale] (int32 accumulators if xs is None)."""
+    scale = tw.scale if xs is not None else None
+    if tw.w2 is not None:
+        return kernels.bitlinear_packed(xq, tw.w2, xs, scale, out_scale=out_scale, out=out, K=K)
+    return kernels.bitlinear_i8(xq, tw.w8, xs, scale, out_scale=out_scale, out=out, K=K)
+
+
 class BitLinear(nn.Module):
     """Linear layer with {-1, 0, 1} weights and int8 activations."""
 
@@ -66,21 +86,24 @@ class BitLinear(nn.Module):
             self.bias = nn.Parameter(torch.zeros(out_features))
         else:
             self.register_parameter("bias", None)
-        self._packed = None  # (wq int8 [N, K16] on device, w_scale fp32 [1] on device, version, device)
+        self._cache = None  # (TernaryWeights, weight version, device)
 
     # -- weight cache -------------------------------------------------------
-    def packed(self, device=None):
-        """(int8 ternary weights [out, in padded to 16], w_scale [1]) on ``device``."""
+    def device_weights(self, device=None) -> TernaryWeights:
+        """The quantised weights on ``device``: int8 [out, in padded to 16],
+        their 2-bit packed copy (packed on the GPU) and the scale."""
         device = torch.device(device) if device is not None else self.weight.device
         ver = self.weight._version
-        p = self._packed
-        if p is None or p[2] != ver or p[3] != device:
+        c = self._cache
+        if c is None or c[1] != ver or c[2] != device:
             wq, scale = weight_quant_ternary(self.weight)
             K16 = _pad16(self.in_features)
             w8 = torch.zeros(self.out_features, K16, dtype=torch.int8)
             w8[:, : self.in_features] = wq.to(torch.int8)
-            self._packed = (w8.to(device), scale.reshape(1).to(device), ver, device)
-        return self._packed[0], self._packed[1]
+            w8 = w8.to(device)
+            w2 = kernels.pack_ternary(w8) if K16 % 64 == 0 else None
+            self._cache = (TernaryWeights(w8, w2, scale.reshape(1).to(device)), ver, device)
+        return self._cache[0]
 
     @torch.no_grad()
     def get_ternary_weights(self) -> Tuple[torch.Tensor, torch.Tensor]:
@@ -100,8 +123,7 @@ class BitLinear(nn.Module):
         K16 = _pad16(K)
         xq = torch.zeros(T, K16, dtype=torch.int8, device=x.device) if K16 != K else None
         xq, xs = kernels.quantize_rows(x2, K, out=xq)
-        w8, ws = self.packed(x.device)
-        y = kernels.bitlinear_i8(xq, w8, xs, ws, K=K16)
+        y = ternary_matmul(xq, self.device_weights(x.device), xs, K=K16)
         if self.bias is not None:
             y = y + self.bias
         return y.view(*lead, self.out_features)

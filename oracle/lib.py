@@ -21,6 +21,7 @@ _lib = None
 _f32p = ctypes.POINTER(ctypes.c_float)
 _i8p = ctypes.POINTER(ctypes.c_int8)
 _i32p = ctypes.POINTER(ctypes.c_int32)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
 _i64p = ctypes.POINTER(ctypes.c_int64)
 _i64 = ctypes.c_int64
 
@@ -49,6 +50,10 @@ def _load():
     lib.orc_bitlinear.restype = None
     lib.orc_bitlinear.argtypes = [_i8p, _i64, _f32p, _i64, _i64, _i8p, ctypes.c_float, _i64, _f32p, _i64,
                                   _i32p, ctypes.c_int]
+    lib.orc_pack_ternary.restype = _i64
+    lib.orc_pack_ternary.argtypes = [_i8p, _i64, _i64, _u8p]
+    lib.orc_unpack_ternary.restype = None
+    lib.orc_unpack_ternary.argtypes = [_u8p, _i64, _i64, _i8p]
     lib.orc_gemm_i8_i32.restype = None
     lib.orc_gemm_i8_i32.argtypes = [_i8p, _i8p, _i32p, _i64, _i64, _i64, ctypes.c_int]
     lib.orc_conv_sqp.restype = None
@@ -132,6 +137,25 @@ def bitlinear(xq, xscale, wq, w_scale, want_acc=False, nthreads=0):
                           float(np.float32(w_scale)), N, _p(out, _f32p), N,
                           _p(acc, _i32p) if want_acc else None, nthreads)
     return (out, acc) if want_acc else out
+
+
+def pack_ternary(W):
+    """int8 ternary [N, K] -> 2-bit packed [N, K/4] uint8 and the count of
+    values outside {-1, 0, 1}."""
+    W = _c(W, np.int8)
+    N, K = W.shape
+    assert K % 16 == 0
+    Wp = np.empty((N, K // 4), np.uint8)
+    bad = _load().orc_pack_ternary(_p(W, _i8p), N, K, _p(Wp, _u8p))
+    return Wp, int(bad)
+
+
+def unpack_ternary(Wp, K):
+    Wp = _c(Wp, np.uint8)
+    N = Wp.shape[0]
+    W = np.empty((N, K), np.int8)
+    _load().orc_unpack_ternary(_p(Wp, _u8p), N, K, _p(W, _i8p))
+    return W
 
 
 def gemm_i8_i32(A, W, nthreads=0):

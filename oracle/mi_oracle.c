@@ -301,6 +301,50 @@ void orc_gemm_i8_i32(const int8_t* A, const int8_t* W, int32_t* C, int64_t M, in
 }
 
 /*
+ * 2-bit packed storage of ternary weights (this build's own format; the
+ * reference keeps the result of weight_quant_ternary, src/rational_bitnet.py:
+ * 63-85, as fp32 and exports it as int8, scripts/export_int8.py:77-81).
+ * Row n of Wp holds K/4 bytes; the little-endian 32-bit word g of the row
+ * holds weights 16g .. 16g+15, weight 16g + 4q + j in bits [p, p+2) with
+ * p = 4j + 2(q & 1) + 16(q >> 1), as a 2-bit two's complement value
+ * (00 = 0, 01 = +1, 11 = -1).
+ * Returns the number of values outside {-1, 0, 1} (stored as 0).
+ */
+int64_t orc_pack_ternary(const int8_t* W, int64_t N, int64_t K, uint8_t* Wp) {
+    int64_t bad = 0;
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t g = 0; g < K / 16; g++) {
+            uint32_t w = 0;
+            for (int e = 0; e < 16; e++) {
+                const int x = W[n * K + 16 * g + e];
+                uint32_t code = 0;
+                if (x == 1) code = 1;
+                else if (x == -1) code = 3;
+                else if (x != 0) bad++;
+                const int q = e >> 2, j = e & 3;
+                w |= code << (4 * j + 2 * (q & 1) + 16 * (q >> 1));
+            }
+            for (int b = 0; b < 4; b++) Wp[n * (K / 4) + 4 * g + b] = (uint8_t)(w >> (8 * b));
+        }
+    }
+    return bad;
+}
+
+/* Inverse of orc_pack_ternary: W [N, K] int8 from Wp [N, K/4]. */
+void orc_unpack_ternary(const uint8_t* Wp, int64_t N, int64_t K, int8_t* W) {
+    for (int64_t n = 0; n < N; n++) {
+        for (int64_t k = 0; k < K; k++) {
+            const int64_t g = k / 16, e = k % 16;
+            const int q = (int)(e >> 2), j = (int)(e & 3);
+            const int p = 4 * j + 2 * (q & 1) + 16 * (q >> 1);
+            const uint8_t byte = Wp[n * (K / 4) + 4 * g + p / 8];
+            const int code = (byte >> (p % 8)) & 3;
+            W[n * K + k] = (int8_t)(code == 3 ? -1 : code == 2 ? -2 : code);
+        }
+    }
+}
+
+/*
  * Causal depthwise conv (nn.Conv1d(D, D, 4, groups=D, padding=3), first L
  * outputs; src/mamba_integer_model.py:378, 404) followed by ste_clamp(-50, 50)
  * and _squareplus_rational (:410-411).  The conv accumulates bias first, then

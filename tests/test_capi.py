@@ -45,5 +45,7 @@ def test_host_side_argument_errors_need_no_gpu(lib):
     # rejected on the host before any CUDA call
     assert lib.mi_scan_i32(None, None, None, None, 15, None, None, None, 1, 1, 16, 16, None) == -1
     assert lib.mi_bitlinear_i8(None, 16, None, None, None, None, None, 16, 16, 16, 16, 0, None) == -1
+    assert lib.mi_bitlinear_packed(None, 16, None, None, None, None, None, 16, 16, 16, 64, 0, None) == -1
+    assert lib.mi_pack_ternary(None, 16, None, 1, 16, None) == -1
     assert lib.mi_version() >= 1
     assert lib.mi_status_string(-2) == b"unsupported shape or configuration"

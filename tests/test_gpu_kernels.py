@@ -175,6 +175,67 @@ def test_gemm_config3_slice(cuda_dev):
     _eq(k.bitlinear_i8(A.to(cuda_dev), Wq.to(cuda_dev)), ref, "config-3 slice")
 
 
+# ---------------------------------------------------------------- 2-bit packed weights
+@pytest.mark.parametrize("N,K", [(80, 1536), (3, 16), (257, 48), (1024, 2048)])
+def test_pack_ternary_matches_oracle(cuda_dev, N, K):
+    from mamba_integer_b200 import _lib
+    k = _mi()
+    g = torch.Generator().manual_seed(N + K)
+    W = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8)
+    ref, bad = orc.pack_ternary(W.numpy())
+    assert bad == 0
+    _eq(k.pack_ternary(W.to(cuda_dev)), ref, "packed bytes")
+    assert _lib.device_error() == 0
+
+
+def test_pack_ternary_flags_non_ternary_values(cuda_dev):
+    from mamba_integer_b200 import _lib
+    k = _mi()
+    W = torch.zeros(2, 32, dtype=torch.int8)
+    W[0, 3], W[1, 17], W[1, 0] = 2, -5, -1
+    ref, bad = orc.pack_ternary(W.numpy())
+    assert bad == 2
+    _lib.device_error()  # clear
+    _eq(k.pack_ternary(W.to(cuda_dev)), ref, "packed bytes with invalid values stored as 0")
+    assert _lib.device_error() & _lib.MI_DEV_PRECOND
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (300, 3072, 768), (1000, 80, 1536), (640, 768, 1536),
+                                   (129, 4096, 256), (512, 96, 64), (200, 32, 192), (130, 256, 2048)])
+def test_gemm_packed_matches_oracle(cuda_dev, M, N, K):
+    k = _mi()
+    g = torch.Generator().manual_seed(M * 5 + N * 11 + K)
+    A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    W = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8)
+    Wp = torch.from_numpy(orc.pack_ternary(W.numpy())[0])
+    ref = orc.gemm_i8_i32(A.numpy(), W.numpy())
+    _eq(k.bitlinear_packed(A.to(cuda_dev), Wp.to(cuda_dev)), ref, "int32 accumulators (packed weights)")
+    xs = (torch.rand(M, generator=g) * 0.05 + 1e-3)
+    ws = torch.tensor([2.0 ** -6])
+    out_ref = orc.bitlinear(A.numpy(), xs.numpy(), W.numpy(), 2.0 ** -6)
+    out = k.bitlinear_packed(A.to(cuda_dev), Wp.to(cuda_dev), xs.to(cuda_dev), ws.to(cuda_dev))
+    _eq(out, out_ref, "scaled fp32 (packed weights)")
+
+
+def test_gemm_packed_config3_slice(cuda_dev):
+    """Config-3 inputs with the weights packed 2 bits each: a 1024-row slice."""
+    from mamba_integer_b200 import synth
+    k = _mi()
+    A, a_scale, Wq, ws = synth.bitlinear_inputs(M=1024, K=2048, N=1024)
+    Wp = k.pack_ternary(Wq.to(cuda_dev))
+    ref = orc.gemm_i8_i32(A.numpy(), Wq.numpy())
+    _eq(k.bitlinear_packed(A.to(cuda_dev), Wp), ref, "config-3 slice, packed weights")
+
+
+def test_gemm_packed_rejects_k_not_multiple_of_64(cuda_dev):
+    from mamba_integer_b200 import _lib
+    k = _mi()
+    A = torch.zeros(128, 48, dtype=torch.int8, device=cuda_dev)
+    Wp = torch.zeros(32, 12, dtype=torch.uint8, device=cuda_dev)
+    with pytest.raises(_lib.MIError, match="status -2"):
+        k.bitlinear_packed(A, Wp)
+
+
 # ---------------------------------------------------------------- conv / ssm / element-wise
 @pytest.mark.parametrize("bsz,L,D", [(2, 37, 512), (1, 130, 1536)])
 def test_conv_act_quant_matches_oracle(cuda_dev, bsz, L, D):
