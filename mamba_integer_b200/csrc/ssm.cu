@@ -129,6 +129,26 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pre
                  : "memory");
 }
 
+// Fast-path update of two states (see the decay comment in ssm_scan_kernel):
+//   dec = min(base/2^15 + mod/2^15, 32000/2^15),  h = h*dec + (1 - dec)*(x*dt*B).
+// The sum, 1 - dec (an FMA with -1: one rounding, as the subtraction) and the
+// three products are f32x2 operations, whose components round exactly as the
+// scalar ones; the final additions stay scalar, because an f32x2 add of two
+// f32x2 products is contracted into an f32x2 FMA by the compiler even with
+// -fmad=false, which would drop the rounding of one product.
+__device__ __forceinline__ void state_pair_fast(float& h0, float& h1, float b0, float b1, float2 ms2, float2 xdt2,
+                                                float B0, float B1) {
+    float2 dec = __fadd2_rn(make_float2(b0, b1), ms2);
+    dec.x = min_nan(dec.x, 0.9765625f);  // 32000 / 2^15
+    dec.y = min_nan(dec.y, 0.9765625f);
+    const float2 om = __ffma2_rn(dec, make_float2(-1.0f, -1.0f), make_float2(1.0f, 1.0f));
+    const float2 u = __fmul2_rn(xdt2, make_float2(B0, B1));
+    const float2 a1 = __fmul2_rn(make_float2(h0, h1), dec);
+    const float2 a2 = __fmul2_rn(om, u);
+    h0 = __fadd_rn(a1.x, a2.x);
+    h1 = __fadd_rn(a1.y, a2.y);
+}
+
 // Inputs of the decay modulation: either the dt_proj output (RW == 0) or the
 // quantised dt rows + scales and the dt_proj weights (RW = words per row).
 struct DtSource {
@@ -330,13 +350,11 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
                 // exact, the sum rounds once, and scaling by 2^-15 commutes with
                 // rounding and with the clamp away from subnormals
                 const float ms = __fmul_rn(mod, 3.0517578125e-05f);
+                // h = h * decay + (1 - decay) * u                       (:309)
 #pragma unroll
-                for (int i = 0; i < NSL; i++) {
-                    const float dec = min_nan(__fadd_rn(bsl[i], ms), 0.9765625f);  // 32000 / 2^15
-                    const float u = __fmul_rn(xdt, Bv[i]);
-                    // h = h * decay + (1 - decay) * u                   (:309)
-                    h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
-                }
+                for (int i = 0; i < NSL; i += 2)
+                    state_pair_fast(h[i], h[i + 1], bsl[i], bsl[i + 1], make_float2(ms, ms), make_float2(xdt, xdt),
+                                    Bv[i], Bv[i + 1]);
             } else {
 #pragma unroll
                 for (int i = 0; i < NSL; i++) {
@@ -544,13 +562,11 @@ ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ b
             const float* Bv = &st.bc[j][sub * NSL];
             if (fast_mask & (1u << j)) {
                 const float ms = __fmul_rn(mod, 3.0517578125e-05f);
+                // h = h * decay + (1 - decay) * u                       (:309)
 #pragma unroll
-                for (int i = 0; i < NSL; i++) {
-                    const float dec = min_nan(__fadd_rn(bsl[i], ms), 0.9765625f);  // 32000 / 2^15
-                    const float u = __fmul_rn(xdt, Bv[i]);
-                    // h = h * decay + (1 - decay) * u                   (:309)
-                    h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
-                }
+                for (int i = 0; i < NSL; i += 2)
+                    state_pair_fast(h[i], h[i + 1], bsl[i], bsl[i + 1], make_float2(ms, ms), make_float2(xdt, xdt),
+                                    Bv[i], Bv[i + 1]);
             } else {
 #pragma unroll
                 for (int i = 0; i < NSL; i++) {
