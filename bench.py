@@ -235,6 +235,51 @@ def secondary_metrics(dev, warmup: int = 3, iters: int = 5):
     return out
 
 
+def decode_metrics(dev, steps: int = 64, warmup: int = 3, batch: int | None = None):
+    """Config 5: greedy decoding of 256 streams after a 512-token Zipf prompt
+    (24 layers, d_model 1024).  The prompt runs through the prefill kernels
+    (untimed); then `steps` decode steps, each replayed from one CUDA graph,
+    are timed with CUDA events.  The state a step reads and writes does not
+    depend on the position, so tok/s over these steps holds for all 512."""
+    from mamba_integer_b200 import synth
+    from mamba_integer_b200.decode import DecodeEngine
+    from mamba_integer_b200.mamba_integer_model import MambaIntegerModel
+
+    hbm, _, src = peaks()
+    c = synth.CONFIGS["c5"]
+    cfg = synth.model_config("c5")
+    B = batch or c["batch"]
+    model = MambaIntegerModel(cfg)
+    model.load_state_dict(synth.model_state_dict(cfg, c["seed"]))
+    model = model.to(dev).eval()
+    prompt = synth.input_ids("c5", B, c["seq_len"]).to(dev)
+    eng = DecodeEngine(model)
+    logits = eng.start(prompt)
+    from mamba_integer_b200 import kernels
+    kernels.argmax_rows(logits, out=eng.ws.next_ids)
+    for _ in range(warmup):
+        eng.step(eng.ws.next_ids)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        eng.step(eng.ws.next_ids)
+    b.record()
+    b.synchronize()
+    ms = a.elapsed_time(b) / steps
+    d, di, L, V, N = cfg["d_model"], 2 * cfg["d_model"], cfg["n_layer"], cfg["vocab_size"], 16
+    R = cfg["ssm_cfg"]["dt_rank"]
+    # algorithmic HBM bytes of one step: scan states and conv windows read and
+    # written, packed weights and the step's logits
+    state = 2 * L * B * di * N * 4 + 2 * L * B * 3 * di * 4
+    weights = L * (2 * di * d + (R + 2 * N) * di + d * di) // 4 + L * di * 64 + V * d // 4
+    nbytes = state + weights + B * V * 4
+    return {"config": f"config5: 24L d1024, {B} streams, 512-token prompt, greedy steps", "steps_timed": steps,
+            "ms_per_step": ms, "tok_per_s": B / ms * 1e3, "hbm_bytes_per_step": nbytes,
+            "achieved_GB_per_s": nbytes / ms / 1e6, "hbm_frac": nbytes / ms / 1e6 / hbm, "peak_source": src,
+            "launches_per_step": DecodeEngine.launches_per_step(L), "cuda_graph": True}
+
+
 def cpu_baseline(n_tokens: int = 256, threads: int = 0):
     """The CPU restatement of the reference path (full 24 layers + lm_head) on
     one sequence of n_tokens of the config-4 workload."""
@@ -401,6 +446,7 @@ def main():
             del logits
             torch.cuda.empty_cache()
             secondary = secondary_metrics(dev)
+            secondary["decode"] = decode_metrics(dev)
 
     hbm, bf16, src = peaks()
     totals = {k: sum(v) for k, v in per_k.items()}

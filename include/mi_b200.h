@@ -194,13 +194,55 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * acc * (w_dt_scale * dts[t]) itself.  R <= 64.
  * split = lanes per channel (1, 2 or 4; 0 = chosen from batch*D vs the SM
  * count): more lanes per channel keep small per-GPU batches occupied.
+ * h_out (optional, [batch, D, N], 16-byte aligned) receives the states after
+ * the last position (the starting point of mi_ssm_step).
  * Replaces: dt_proj + DyadicScanFunction section, src/mamba_integer_model.py:419-444
  * (BitLinear rescale: src/rational_bitnet.py:204-208).
  */
 int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const int8_t* dtq, int ldq,
                    const float* dts, const int8_t* w_dt, const float* w_dt_scale, int R,
-                   const float* z, int ldz, const float* base, float* y, float* amax, int batch,
-                   int L, int D, int N, int split, void* stream);
+                   const float* z, int ldz, const float* base, float* y, float* amax, float* h_out,
+                   int batch, int L, int D, int N, int split, void* stream);
+
+/*
+ * Decode: one new position for `batch` independent streams (one CTA per
+ * stream).  The reference has no step API; it recomputes
+ * MambaIntegerModel.forward over the whole sequence for every token
+ * (scripts/inference.py:148-160).  These steps give the bits that forward
+ * gives the last position: same operations, same order.
+ *
+ * mi_conv_step: x_t = first D columns of xz row b (row stride ldx); win
+ * [batch, 3, D] holds x_{t-3}, x_{t-2}, x_{t-1} and is advanced in place;
+ * act (optional) [batch, D] = squareplus(ste_clamp(conv, +-50)); xq [batch, D]
+ * int8 and xscale [batch] its quantisation.  D % 4 == 0, D <= 4096.
+ * Replaces: conv1d + fused_squareplus_clamp at the last position,
+ * src/mamba_integer_model.py:404-411 (and launch_conv1d_step,
+ * src/cuda_kernels/conv1d_step.cu:61-78, whose bias-last order differs).
+ */
+int mi_conv_step(const float* xz, int ldx, const float* w, const float* bias, float* win, float* act,
+                 int8_t* xq, float* xscale, int batch, int D, void* stream);
+
+/*
+ * mi_ssm_step: xp row b (stride ldxp) = [dt (R) | B (N) | C (N)], the x_proj
+ * output; the dt row is quantised (activation_quant_dynamic), dt_proj is the
+ * exact int32 dot product with w_dt int8 [D, R16] and its rescale, then
+ * decay / dt / u, one convex update of h [batch, D, N] (in place), y = sum h*C,
+ * the gate with z (row stride ldz); y (optional) [batch, D] and its int8
+ * quantisation xq [batch, D], xscale [batch].  N == 16, D <= 4096, R <= 64.
+ * Replaces: the dt_proj + DyadicScanFunction section at the last position,
+ * src/mamba_integer_model.py:419-444.
+ */
+int mi_ssm_step(const float* act, const float* xp, int ldxp, int R, const int8_t* w_dt,
+                const float* w_dt_scale, const float* z, int ldz, const float* base, float* h, float* y,
+                int8_t* xq, float* xscale, int batch, int D, int N, void* stream);
+
+/*
+ * mi_argmax_rows: out[t] = torch.argmax(x[t, :V]) (first index of the
+ * maximum; NaN counts as the maximum), x rows of stride ldx.
+ * Replaces the greedy choice over logits[:, -1, :] in the generation loop,
+ * scripts/inference.py:150-158 (which samples with temperature 0.8).
+ */
+int mi_argmax_rows(const float* x, int ldx, int T, int V, int64_t* out, void* stream);
 
 /* Convex dyadic scan on materialised inputs: h = h*(n/2^15) + (1-n/2^15)*u.
  * u, nums, h [batch, L, DN].

@@ -1,0 +1,302 @@
+// decode.cu -- one generated token for a batch of independent streams:
+//   * conv_step_kernel: the causal depthwise conv at the newest position from
+//     a per-stream window of the 3 previous conv inputs, ste_clamp +
+//     squareplus, int8 quantisation of the row; the window advances;
+//   * ssm_step_kernel: int8 quantisation of the step's dt row, the fused
+//     dt_proj dot products, decay / dt / u, one convex dyadic update of the
+//     16 fp32 states per channel (kept per stream in HBM), y = sum_n h*C, the
+//     gate and the int8 quantisation of y;
+//   * argmax_rows_kernel: greedy token choice over the logits.
+// One CTA per stream: a stream's row never leaves its CTA, so the row absmax
+// of each quantisation is a block reduction instead of an atomic.
+//
+// Every operation is the prefill kernels' own, in the same order, so a token
+// decoded here gets the bits MambaIntegerModel.forward gives the last position
+// of the full sequence (src/mamba_integer_model.py:396-447, :486-495) -- the
+// reference decodes by recomputing that forward for every new token
+// (scripts/inference.py:148-160).  The conv keeps the model's order (bias
+// first, then one FMA per tap), not the bias-last sum of
+// src/cuda_kernels/conv1d_step.cu:30-57.
+#include "mi_common.cuh"
+
+namespace mi {
+namespace decode {
+
+constexpr int STEP_THREADS = 256;
+constexpr int MAX_D = 4096;  // channels per stream row
+constexpr int CONV_CHUNKS = MAX_D / 4 / STEP_THREADS;   // float4 chunks per thread
+constexpr int SSM_CH = MAX_D / STEP_THREADS;            // channels per thread
+constexpr int MAX_R16 = 64;                             // dt_rank padded to 16
+
+// activation_quant_dynamic's scale (src/rational_bitnet.py:102-111), as the
+// row kernels compute it: s = max(amax, 1e-8), inv = reciprocal(s) * 127.
+__device__ __forceinline__ float quant_inv(float amax, float& xscale) {
+    const float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
+    xscale = __fdiv_rn(sc, 127.0f);
+    return __fmul_rn(__frcp_rn(sc), 127.0f);
+}
+
+// Block-wide max of non-negative fp32 bit patterns (NaN sorts above +inf).
+__device__ __forceinline__ unsigned block_max_u32(unsigned m, unsigned* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = lane < STEP_THREADS / 32 ? red[lane] : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+// xz row b: the first D columns are the conv input x_t; win [batch, 3, D]:
+// x_{t-3}, x_{t-2}, x_{t-1}.  D % 4 == 0, D <= MAX_D.
+__global__ void __launch_bounds__(STEP_THREADS)
+conv_step_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w, const float* __restrict__ bias,
+                 float* __restrict__ win, float* __restrict__ act, int8_t* __restrict__ xq,
+                 float* __restrict__ xscale, int D) {
+    __shared__ unsigned red[STEP_THREADS / 32];
+    const int b = blockIdx.x;
+    const float* xrow = xz + (size_t)b * ldx;
+    float* wrow = win + (size_t)b * 3 * D;
+    float4 a[CONV_CHUNKS];
+    unsigned m = 0u;
+#pragma unroll
+    for (int i = 0; i < CONV_CHUNKS; i++) {
+        const int c = 4 * (threadIdx.x + i * STEP_THREADS);
+        if (c < D) {
+            const float4 x0 = *reinterpret_cast<const float4*>(wrow + c);
+            const float4 x1 = *reinterpret_cast<const float4*>(wrow + D + c);
+            const float4 x2 = *reinterpret_cast<const float4*>(wrow + 2 * D + c);
+            const float4 x3 = *reinterpret_cast<const float4*>(xrow + c);
+            const float4 bs = *reinterpret_cast<const float4*>(bias + c);
+            float r[4];
+            const float xs0[4] = {x0.x, x0.y, x0.z, x0.w}, xs1[4] = {x1.x, x1.y, x1.z, x1.w};
+            const float xs2[4] = {x2.x, x2.y, x2.z, x2.w}, xs3[4] = {x3.x, x3.y, x3.z, x3.w};
+            const float bv[4] = {bs.x, bs.y, bs.z, bs.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float4 wc = *reinterpret_cast<const float4*>(w + 4 * (c + e));
+                // bias first, then one FMA per tap k = 0..3 over positions t-3+k
+                float acc = bv[e];
+                acc = __fmaf_rn(wc.x, xs0[e], acc);
+                acc = __fmaf_rn(wc.y, xs1[e], acc);
+                acc = __fmaf_rn(wc.z, xs2[e], acc);
+                acc = __fmaf_rn(wc.w, xs3[e], acc);
+                r[e] = squareplus_bounded(ste_clamp(acc, -50.0f, 50.0f));
+                m = max(m, __float_as_uint(fabsf(r[e])));
+            }
+            a[i] = make_float4(r[0], r[1], r[2], r[3]);
+            // advance the window
+            *reinterpret_cast<float4*>(wrow + c) = x1;
+            *reinterpret_cast<float4*>(wrow + D + c) = x2;
+            *reinterpret_cast<float4*>(wrow + 2 * D + c) = x3;
+            if (act) *reinterpret_cast<float4*>(act + (size_t)b * D + c) = a[i];
+        }
+    }
+    const float amax = __uint_as_float(block_max_u32(m, red));
+    float xs;
+    const float inv = quant_inv(amax, xs);
+#pragma unroll
+    for (int i = 0; i < CONV_CHUNKS; i++) {
+        const int c = 4 * (threadIdx.x + i * STEP_THREADS);
+        if (c < D) {
+            const char4 q = make_char4((signed char)quant_i8(__fmul_rn(a[i].x, inv)),
+                                       (signed char)quant_i8(__fmul_rn(a[i].y, inv)),
+                                       (signed char)quant_i8(__fmul_rn(a[i].z, inv)),
+                                       (signed char)quant_i8(__fmul_rn(a[i].w, inv)));
+            *reinterpret_cast<char4*>(xq + (size_t)b * D + c) = q;
+        }
+    }
+    if (threadIdx.x == 0) xscale[b] = xs;
+}
+
+// One step of the selective scan for stream b (blockIdx.x).
+//   xp row b = [dt (R) | B (16) | C (16)] (the x_proj output, row stride ldxp);
+//   act [batch, D]; z rows stride ldz; base [D, 16]; w_dt int8 [D, R16];
+//   h [batch, D, 16] fp32 states, updated in place;
+//   y (optional) [batch, D]; xq [batch, D] int8 and xscale [batch]: y quantised.
+__global__ void __launch_bounds__(STEP_THREADS)
+ssm_step_kernel(const float* __restrict__ act, const float* __restrict__ xp, int ldxp, int R,
+                const int8_t* __restrict__ w_dt, const float* __restrict__ w_dt_scale, const float* __restrict__ z,
+                int ldz, const float* __restrict__ base, float* __restrict__ h, float* __restrict__ y,
+                int8_t* __restrict__ xq, float* __restrict__ xscale, int D) {
+    constexpr int NS = 16;
+    __shared__ __align__(16) int32_t dtq_s[MAX_R16 / 4];
+    __shared__ float bc_s[2 * NS];
+    __shared__ float dts_s;
+    __shared__ unsigned red[STEP_THREADS / 32];
+    const int b = blockIdx.x;
+    const float* row = xp + (size_t)b * ldxp;
+    const int R16 = (R + 15) / 16 * 16;
+    if (threadIdx.x < 32) {
+        // activation_quant_dynamic of the dt row, as mi_quantize_rows computes it
+        const int lane = threadIdx.x;
+        float am = 0.0f;
+        bool nan = false;
+        for (int k = lane; k < R; k += 32) {
+            const float v = fabsf(row[k]);
+            nan |= (v != v);
+            am = fmaxf(am, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        nan = __any_sync(0xffffffffu, nan);
+        const float amax = nan ? __int_as_float(0x7fc00000) : am;
+        float xs;
+        const float inv = quant_inv(amax, xs);
+        int8_t* q8 = reinterpret_cast<int8_t*>(dtq_s);
+        for (int k = lane; k < R16; k += 32) q8[k] = k < R ? (int8_t)quant_i8(__fmul_rn(row[k], inv)) : (int8_t)0;
+        if (lane == 0) dts_s = xs;
+        bc_s[lane] = row[R + lane];  // B (16) then C (16)
+    }
+    __syncthreads();
+    const float wsc = *w_dt_scale;
+    const float dscale = __fmul_rn(wsc, dts_s);  // (w_scale * x_scale) of the dt_proj BitLinear
+    float yv[SSM_CH];
+    unsigned m = 0u;
+#pragma unroll
+    for (int i = 0; i < SSM_CH; i++) {
+        const int c = threadIdx.x + i * STEP_THREADS;
+        yv[i] = 0.0f;
+        if (c >= D) continue;
+        // dt_proj: exact int32 dot product, then the BitLinear rescale
+        const int4* wq = reinterpret_cast<const int4*>(w_dt + (size_t)c * R16);
+        int acc = 0;
+        for (int k = 0; k < R16 / 16; k++) {
+            const int4 wv = wq[k];
+            acc = __dp4a(dtq_s[4 * k], wv.x, acc);
+            acc = __dp4a(dtq_s[4 * k + 1], wv.y, acc);
+            acc = __dp4a(dtq_s[4 * k + 2], wv.z, acc);
+            acc = __dp4a(dtq_s[4 * k + 3], wv.w, acc);
+        }
+        const float mod = ste_clamp(__fmul_rn((float)acc, dscale), -20.0f, 20.0f);       // (:419-421)
+        const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);  // (:425-427)
+        const float xdt = __fmul_rn(act[(size_t)b * D + c], dtv);
+        float4* hp = reinterpret_cast<float4*>(h + ((size_t)b * D + c) * NS);
+        const float4* bp = reinterpret_cast<const float4*>(base + (size_t)c * NS);
+        float yacc = 0.0f;
+#pragma unroll
+        for (int q = 0; q < NS / 4; q++) {
+            const float4 hv4 = hp[q], bv4 = bp[q];
+            float hv[4] = {hv4.x, hv4.y, hv4.z, hv4.w};
+            const float bv[4] = {bv4.x, bv4.y, bv4.z, bv4.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int n = 4 * q + e;
+                // decay_nums = ste_clamp(base + mod, 0, 32000); decay = nums / 2^15   (:423-424, :305)
+                const float num = ste_clamp(__fadd_rn(bv[e], mod), 0.0f, 32000.0f);
+                const float dec = __fmul_rn(num, 3.0517578125e-05f);
+                const float u = __fmul_rn(xdt, bc_s[n]);
+                hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));  // (:309)
+                yacc = __fmaf_rn(hv[e], bc_s[NS + n], yacc);                                 // (:440)
+            }
+            hp[q] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        }
+        yv[i] = sigmoid_gate(yacc, z[(size_t)b * ldz + c]);                                  // (:441-444)
+        if (y) y[(size_t)b * D + c] = yv[i];
+        m = max(m, __float_as_uint(fabsf(yv[i])));
+    }
+    const float amax = __uint_as_float(block_max_u32(m, red));
+    float xs;
+    const float inv = quant_inv(amax, xs);
+#pragma unroll
+    for (int i = 0; i < SSM_CH; i++) {
+        const int c = threadIdx.x + i * STEP_THREADS;
+        if (c < D) xq[(size_t)b * D + c] = (int8_t)quant_i8(__fmul_rn(yv[i], inv));
+    }
+    if (threadIdx.x == 0) xscale[b] = xs;
+}
+
+// torch.argmax over each row: the first index of the maximum, NaN above
+// every number (the first NaN wins).
+__device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) {
+    const bool vn = v != v, bn = bv != bv;
+    if (vn || bn) return vn && (!bn || i < bi);
+    return v > bv || (v == bv && i < bi);
+}
+
+__global__ void __launch_bounds__(STEP_THREADS)
+argmax_rows_kernel(const float* __restrict__ x, int ldx, int V, int64_t* __restrict__ out) {
+    __shared__ float sv[STEP_THREADS / 32];
+    __shared__ int si[STEP_THREADS / 32];
+    const float* row = x + (size_t)blockIdx.x * ldx;
+    float bv = -__int_as_float(0x7f800000);
+    int bi = 0x7fffffff;
+    for (int k = threadIdx.x; k < V; k += STEP_THREADS) {
+        const float v = row[k];
+        if (argmax_better(v, k, bv, bi)) {
+            bv = v;
+            bi = k;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (argmax_better(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        bv = lane < STEP_THREADS / 32 ? sv[lane] : -__int_as_float(0x7f800000);
+        bi = lane < STEP_THREADS / 32 ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (argmax_better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        // a row of -inf only: every element ties, index 0
+        if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+}  // namespace decode
+}  // namespace mi
+
+extern "C" int mi_conv_step(const float* xz, int ldx, const float* w, const float* bias, float* win, float* act,
+                            int8_t* xq, float* xscale, int batch, int D, void* stream) {
+    using namespace mi::decode;
+    if (!xz || !w || !bias || !win || !xq || !xscale) return MI_ERR_INVALID;
+    if (batch <= 0 || D <= 0 || ldx < D) return MI_ERR_INVALID;
+    if (D % 4 != 0 || D > MAX_D || ldx % 4 != 0 || batch > 2147483647 / 4) return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)xz | (uintptr_t)w | (uintptr_t)bias | (uintptr_t)win | (uintptr_t)act) & 15) return MI_ERR_INVALID;
+    if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
+    conv_step_kernel<<<batch, STEP_THREADS, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, win, act, xq, xscale, D);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+extern "C" int mi_ssm_step(const float* act, const float* xp, int ldxp, int R, const int8_t* w_dt,
+                           const float* w_dt_scale, const float* z, int ldz, const float* base, float* h, float* y,
+                           int8_t* xq, float* xscale, int batch, int D, int N, void* stream) {
+    using namespace mi::decode;
+    if (!act || !xp || !w_dt || !w_dt_scale || !z || !base || !h || !xq || !xscale) return MI_ERR_INVALID;
+    if (N != 16) return MI_ERR_UNSUPPORTED;
+    if (batch <= 0 || D <= 0 || R <= 0 || ldxp < R + 2 * N || ldz < D) return MI_ERR_INVALID;
+    if (D > MAX_D || (R + 15) / 16 * 16 > MAX_R16) return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)h | (uintptr_t)base | (uintptr_t)w_dt) & 15) return MI_ERR_INVALID;
+    ssm_step_kernel<<<batch, STEP_THREADS, 0, (cudaStream_t)stream>>>(act, xp, ldxp, R, w_dt, w_dt_scale, z, ldz, base,
+                                                                     h, y, xq, xscale, D);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+extern "C" int mi_argmax_rows(const float* x, int ldx, int T, int V, int64_t* out, void* stream) {
+    using namespace mi::decode;
+    if (!x || !out || T <= 0 || V <= 0 || ldx < V) return MI_ERR_INVALID;
+    argmax_rows_kernel<<<T, STEP_THREADS, 0, (cudaStream_t)stream>>>(x, ldx, V, out);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}

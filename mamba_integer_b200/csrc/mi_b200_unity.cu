@@ -6,4 +6,5 @@
 #include "rowops.cu"
 #include "ssm.cu"
 #include "gemm_i8.cu"
+#include "decode.cu"
 #include "noalloc.cu"

@@ -226,7 +226,7 @@ template <int RW, int S>
 __global__ void __launch_bounds__(SCAN_THREADS, 21)
 ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
                 const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
-                float* __restrict__ amax, int L, int D) {
+                float* __restrict__ amax, float* __restrict__ h_out, int L, int D) {
     constexpr int CHW = 32 / S;   // channels per warp
     constexpr int NSL = NS / S;   // states per lane
     __shared__ __align__(16) ScanStage stage[SSTAGES];
@@ -405,6 +405,12 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
         __syncwarp();  // the buffer is refilled by the next iteration's copies
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    if (h_out && active) {
+        // final states of the sequence [batch, D, 16] (the decode steps continue from them)
+        float4* dst = reinterpret_cast<float4*>(h_out + ((size_t)b * D + d) * NS + sub * NSL);
+#pragma unroll
+        for (int i = 0; i < NSL / 4; i++) dst[i] = make_float4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -460,7 +466,7 @@ template <int RW, int S>
 __global__ void __launch_bounds__(SCAN_THREADS)
 ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
                       const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
-                      float* __restrict__ amax, int L, int D) {
+                      float* __restrict__ amax, float* __restrict__ h_out, int L, int D) {
     static_assert(S == 2 || S == 4, "split variant");
     constexpr int CHW = 32 / S;   // channels per warp
     constexpr int NSL = NS / S;   // states per lane
@@ -631,6 +637,12 @@ ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ b
         __syncwarp();  // the buffers are refilled by the next iteration
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    if (h_out && active) {
+        // final states of the sequence [batch, D, 16] (the decode steps continue from them)
+        float4* dst = reinterpret_cast<float4*>(h_out + ((size_t)b * D + d) * NS + sub * NSL);
+#pragma unroll
+        for (int i = 0; i < NSL / 4; i++) dst[i] = make_float4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+    }
 }
 
 }  // namespace ssm
@@ -678,15 +690,17 @@ static int pick_split(int batch, int D) {
 template <int RW>
 static void launch_scan(int split, int batch, int L, int D, const float* act, const float* bc, int ldbc,
                         const DtSource& src, const float* z, int ldz, const float* base, float* y, float* amax,
-                        cudaStream_t s) {
+                        float* h_out, cudaStream_t s) {
     const int chw = SCAN_THREADS / split;
     dim3 grid(cdiv(D, chw), batch);
     if (split == 1)
-        ssm_scan_kernel<RW, 1><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, L, D);
+        ssm_scan_kernel<RW, 1><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
     else if (split == 2)
-        ssm_scan_split_kernel<RW, 2><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, L, D);
+        ssm_scan_split_kernel<RW, 2><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out,
+                                                                   L, D);
     else
-        ssm_scan_split_kernel<RW, 4><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, L, D);
+        ssm_scan_split_kernel<RW, 4><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out,
+                                                                   L, D);
 }
 
 }  // namespace ssm
@@ -703,15 +717,15 @@ extern "C" int mi_ssm_scan(const float* act, const float* bc, int ldbc, const fl
     if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
     mi::ssm::DtSource src{modraw, nullptr, 0, nullptr, nullptr, nullptr};
     mi::ssm::launch_scan<0>(mi::ssm::pick_split(batch, D), batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax,
-                            (cudaStream_t)stream);
+                            nullptr, (cudaStream_t)stream);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
 
 extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const int8_t* dtq, int ldq, const float* dts,
                               const int8_t* w_dt, const float* w_dt_scale, int R, const float* z, int ldz,
-                              const float* base, float* y, float* amax, int batch, int L, int D, int N, int split,
-                              void* stream) {
+                              const float* base, float* y, float* amax, float* h_out, int batch, int L, int D, int N,
+                              int split, void* stream) {
     if (!act || !bc || !dtq || !dts || !w_dt || !w_dt_scale || !z || !base || !y) return MI_ERR_INVALID;
     if (N != mi::ssm::NS) return MI_ERR_UNSUPPORTED;
     if (batch <= 0 || L <= 0 || D <= 0 || R <= 0 || ldbc < 2 * N || ldz < D) return MI_ERR_INVALID;
@@ -722,15 +736,16 @@ extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const
     if (((uintptr_t)act | (uintptr_t)bc | (uintptr_t)z | (uintptr_t)dtq | (uintptr_t)w_dt) & 15)
         return MI_ERR_UNSUPPORTED;
     if (((uintptr_t)dts) & 3) return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)h_out) & 15) return MI_ERR_INVALID;
     if ((D | ldbc | ldz) & 3) return MI_ERR_UNSUPPORTED;
     if (split == 0) split = mi::ssm::pick_split(batch, D);
     mi::ssm::DtSource src{nullptr, dtq, ldq, dts, w_dt, w_dt_scale};
     cudaStream_t s = (cudaStream_t)stream;
     switch (R16 / 4) {
-        case 4: mi::ssm::launch_scan<4>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
-        case 8: mi::ssm::launch_scan<8>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
-        case 12: mi::ssm::launch_scan<12>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
-        case 16: mi::ssm::launch_scan<16>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, s); break;
+        case 4: mi::ssm::launch_scan<4>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, h_out, s); break;
+        case 8: mi::ssm::launch_scan<8>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, h_out, s); break;
+        case 12: mi::ssm::launch_scan<12>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, h_out, s); break;
+        case 16: mi::ssm::launch_scan<16>(split, batch, L, D, act, bc, ldbc, src, z, ldz, base, y, amax, h_out, s); break;
         default: return MI_ERR_UNSUPPORTED;
     }
     MI_CHECK_LAUNCH();

@@ -85,7 +85,7 @@ def launches_per_forward(n_layer: int) -> int:
 
 
 def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N: int, timer=NO_TIMER,
-              scan_split: int = 0):
+              scan_split: int = 0, h_out=None):
     """Everything between the in_proj output (ws.xz) and the out_proj output (ws.out)."""
     with timer("conv_act_quant"):
         kernels.conv_act_quant(ws.xz, p["conv_w"], p["conv_b"], batch, L, di, act=ws.act, xq=ws.xq_i,
@@ -98,7 +98,7 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
         # dt_proj is fused into the scan (each channel's dot product by dp4a)
         ws.amax.zero_()
         kernels.ssm_scan_dt(ws.act, ws.xp[:, R:], ws.dtq, ws.dts, p["w_dt"].w8, p["w_dt"].scale, R, ws.xz[:, di:],
-                            p["base"], batch, L, y=ws.y, amax=ws.amax, split=scan_split)
+                            p["base"], batch, L, y=ws.y, amax=ws.amax, split=scan_split, h_out=h_out)
     with timer("quant_y"):
         kernels.quantize_rows(ws.y, out=ws.xq_i, xscale=ws.xs_i, amax=ws.amax)
     with timer("gemm_out_proj"):
@@ -147,9 +147,13 @@ class PrefillEngine:
             self._ws[key] = _Workspace(batch * L, self.d, self.di, self.R, self.N, self.dev)
         return self._ws[key]
 
-    def forward(self, input_ids: torch.Tensor, logits: torch.Tensor | None = None, timer=NO_TIMER) -> torch.Tensor:
-        """Logits [batch, L, vocab] for int64 ids [batch, L] on this engine's device.
-        ``timer(name)`` (a context manager factory) brackets each kernel launch."""
+    def forward(self, input_ids: torch.Tensor, logits: torch.Tensor | None = None, timer=NO_TIMER, states=None,
+                last_only: bool = False) -> torch.Tensor:
+        """Logits [batch, L, vocab] for int64 ids [batch, L] on this engine's device
+        ([batch, vocab] of the last position with ``last_only``).
+        ``timer(name)`` (a context manager factory) brackets each kernel launch.
+        ``states`` (a decode.StreamStates for this batch) receives each layer's
+        conv window and final scan states, for decoding after the prompt."""
         batch, L = input_ids.shape
         T = batch * L
         d, di, R, N, V = self.d, self.di, self.R, self.N, self.V
@@ -164,12 +168,24 @@ class PrefillEngine:
         for i, p in enumerate(self.layers):
             with timer("gemm_in_proj"):
                 ternary_matmul(ws.xq_d, p["w_in"], ws.xs_d, out=ws.xz)
-            _ssm_half(p, ws, batch, L, d, di, R, N, timer, self.scan_split)
+            if states is not None:
+                states.capture_window(i, ws.xz, batch, L)
+            _ssm_half(p, ws, batch, L, d, di, R, N, timer, self.scan_split,
+                      h_out=states.h[i] if states is not None else None)
             nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
             g, s = (nxt["gamma"], nxt["step"]) if nxt else (self.gamma_f, self.step_f)
             with timer("rowprep"):
                 kernels.rowprep(g, s, T, d, x=ws.x, delta=ws.out, res_gate=p["res_gate"], x_out=ws.x,
                                 xq=ws.xq_d, xscale=ws.xs_d)
+        if last_only:
+            # norm_f rows of the last positions only: A rows of stride L*d, their scales gathered
+            xq_last = ws.xq_d.view(batch, L, d)[:, L - 1, :]
+            xs_last = ws.xs_d.view(batch, L)[:, L - 1].contiguous()
+            if logits is None:
+                logits = torch.empty(batch, V, dtype=torch.float32, device=self.dev)
+            with timer("gemm_lm_head"):
+                ternary_matmul(xq_last, self.w_lm, xs_last, out_scale=self.out_scale, out=logits.view(batch, V))
+            return logits.view(batch, V)
         if logits is None:
             logits = torch.empty(T, V, dtype=torch.float32, device=self.dev)
         with timer("gemm_lm_head"):

@@ -224,19 +224,54 @@ def ssm_scan(act, bc, modraw, z, base, batch: int, L: int, y=None, amax=None):
 
 
 def ssm_scan_dt(act, bc, dtq, dts, w_dt, w_dt_scale, R: int, z, base, batch: int, L: int, y=None, amax=None,
-                split: int = 0):
+                split: int = 0, h_out=None):
     """ssm_scan with dt_proj fused (see mi_ssm_scan_dt): dtq int8 [T, ldq] quantised
     dt rows, dts [T] their scales, w_dt int8 [D, ceil16(R)], w_dt_scale [1].
-    split: lanes per channel (0 = automatic)."""
+    split: lanes per channel (0 = automatic); h_out [batch, D, N]: final states."""
     D, N = base.shape
     T = batch * L
     if y is None:
         y = torch.empty(T, D, dtype=torch.float32, device=act.device)
     _lib.check(_lib.load().mi_ssm_scan_dt(act.data_ptr(), bc.data_ptr(), bc.stride(0), dtq.data_ptr(), dtq.stride(0),
                                           dts.data_ptr(), w_dt.data_ptr(), w_dt_scale.data_ptr(), R, z.data_ptr(),
-                                          z.stride(0), base.data_ptr(), y.data_ptr(), _ptr(amax), batch, L, D, N,
-                                          int(split), _stream()), "mi_ssm_scan_dt")
+                                          z.stride(0), base.data_ptr(), y.data_ptr(), _ptr(amax), _ptr(h_out), batch,
+                                          L, D, N, int(split), _stream()), "mi_ssm_scan_dt")
     return y
+
+
+# ---------------------------------------------------------------------------
+# decode steps
+# ---------------------------------------------------------------------------
+def conv_step(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, win: torch.Tensor, D: int, xq: torch.Tensor,
+              xscale: torch.Tensor, act: Optional[torch.Tensor] = None):
+    """One causal-conv position per stream: xz rows [batch, >=D] (x_t = first D
+    columns), win [batch, 3, D] advanced in place; writes act (optional), xq, xscale."""
+    batch = xz.shape[0]
+    _lib.check(_lib.load().mi_conv_step(xz.data_ptr(), xz.stride(0), w.data_ptr(), bias.data_ptr(), win.data_ptr(),
+                                        _ptr(act), xq.data_ptr(), xscale.data_ptr(), batch, D, _stream()),
+               "mi_conv_step")
+
+
+def ssm_step(act, xp, R: int, w_dt, w_dt_scale, z, base, h, xq, xscale, y=None):
+    """One selective-scan position per stream (see mi_ssm_step); h [batch, D, 16]
+    is updated in place; writes y (optional), xq, xscale."""
+    batch, D = act.shape
+    N = base.shape[1]
+    _lib.check(_lib.load().mi_ssm_step(act.data_ptr(), xp.data_ptr(), xp.stride(0), R, w_dt.data_ptr(),
+                                       w_dt_scale.data_ptr(), z.data_ptr(), z.stride(0), base.data_ptr(), h.data_ptr(),
+                                       _ptr(y), xq.data_ptr(), xscale.data_ptr(), batch, D, N, _stream()),
+               "mi_ssm_step")
+
+
+def argmax_rows(x: torch.Tensor, V: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """torch.argmax(x[:, :V], dim=-1) as int64 (first index of the maximum, NaN highest)."""
+    T = x.shape[0]
+    V = x.shape[1] if V is None else V
+    if out is None:
+        out = torch.empty(T, dtype=torch.int64, device=x.device)
+    _lib.check(_lib.load().mi_argmax_rows(x.data_ptr(), x.stride(0), T, V, out.data_ptr(), _stream()),
+               "mi_argmax_rows")
+    return out
 
 
 def scan_convex(u: torch.Tensor, nums: torch.Tensor) -> torch.Tensor:

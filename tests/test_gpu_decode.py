@@ -1,0 +1,113 @@
+"""Decoding on the GPU against the CPU oracle.
+
+The reference decodes by recomputing MambaIntegerModel.forward over the whole
+sequence for every token (scripts/inference.py:148-160).  So the check for
+each step is: its logits equal, bit for bit, the oracle's full forward over
+prompt + tokens so far at the last position, and the greedy token is that
+row's first maximum.
+"""
+import numpy as np
+import pytest
+import torch
+
+import cases
+from oracle import lib as orc
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(cfg, sd, dev):
+    from mamba_integer_b200.mamba_integer_model import MambaIntegerModel
+    m = MambaIntegerModel(cfg)
+    m.load_state_dict(sd)
+    return m.to(dev).eval()
+
+
+def _first_argmax(a):
+    return np.argmax(a, axis=-1)  # first index of the maximum (no NaN in these logits)
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+@pytest.mark.parametrize("name,batch,prompt,n_new", [("c1", 3, 20, 5), ("c5s", 2, 2, 4)])
+def test_greedy_decode_equals_full_recompute(cuda_dev, use_graph, name, batch, prompt, n_new):
+    from mamba_integer_b200 import synth
+    from mamba_integer_b200.decode import DecodeEngine
+    from oracle import model as om
+    cfg, sd, _ = cases.model_inputs(name)
+    ids = synth.input_ids(cases.MODEL_CASES[name]["base"], batch, prompt)
+    m = _model(cfg, sd, cuda_dev)
+    eng = DecodeEngine(m, use_graph=use_graph)
+    p = om.prepare(sd)
+    seq = ids.numpy()
+    logits = eng.start(ids.to(cuda_dev)).cpu().numpy()
+    for t in range(n_new):
+        ref = om.forward(p, cfg, seq)[:, -1, :]
+        bad = logits.view(np.uint32) != ref.view(np.uint32)
+        assert not bad.any(), f"step {t}: {int(bad.sum())} logits differ from the full recompute"
+        nxt = _first_argmax(ref)
+        if t == 0:
+            from mamba_integer_b200 import kernels
+            got = kernels.argmax_rows(torch.from_numpy(logits).to(cuda_dev)).cpu().numpy()
+        else:
+            got = eng.next_ids().cpu().numpy()
+        assert (got == nxt).all(), f"step {t}: greedy ids {got} vs {nxt}"
+        seq = np.concatenate([seq, nxt[:, None]], axis=1)
+        logits = eng.step(torch.from_numpy(nxt).to(cuda_dev)).cpu().numpy()
+
+
+def test_generate_matches_stepwise_oracle(cuda_dev):
+    from mamba_integer_b200 import synth
+    from mamba_integer_b200.decode import DecodeEngine
+    from oracle import model as om
+    cfg, sd, _ = cases.model_inputs("c1")
+    ids = synth.input_ids("c1", 2, 9)
+    m = _model(cfg, sd, cuda_dev)
+    out = DecodeEngine(m).generate(ids.to(cuda_dev), 4).cpu().numpy()
+    p = om.prepare(sd)
+    seq = ids.numpy()
+    for t in range(4):
+        nxt = _first_argmax(om.forward(p, cfg, seq)[:, -1, :])
+        assert (out[:, t] == nxt).all(), t
+        seq = np.concatenate([seq, nxt[:, None]], axis=1)
+
+
+def test_prefill_final_states_match_oracle(cuda_dev):
+    """h_out of the fused scan = the oracle's state after the last position."""
+    from mamba_integer_b200 import kernels
+    bsz, L, D, R = 2, 37, 160, 16
+    g = torch.Generator().manual_seed(5)
+    act = (torch.rand(bsz * L, D, generator=g) * 3).float()
+    bc = (torch.randn(bsz * L, 2 * 16, generator=g)).float()
+    dt = (torch.randn(bsz * L, R, generator=g)).float()
+    z = (torch.randn(bsz * L, D, generator=g) * 2).float()
+    base = torch.randint(29492, 32736, (D, 16), generator=g).float()
+    wdt = torch.randint(-1, 2, (D, R), generator=g, dtype=torch.int8)
+    ws = 2.0 ** -6
+    dtq, dts = orc.quant_rows(dt.numpy())
+    modraw = orc.bitlinear(dtq, dts, wdt.numpy(), ws)
+    y_ref, h_ref = orc.ssm(act.numpy(), bc.numpy(), modraw, z.numpy(), base.numpy(), bsz, L, want_h=True)
+    dv = lambda t: t.to(cuda_dev)  # noqa: E731
+    dtq_d = torch.zeros(bsz * L, 16, dtype=torch.int8)
+    dtq_d[:, :R] = torch.from_numpy(dtq)
+    h = torch.full((bsz, D, 16), float("nan"), device=cuda_dev)
+    for split in (1, 2, 4):
+        y = kernels.ssm_scan_dt(dv(act), dv(bc), dv(dtq_d), dv(torch.from_numpy(dts)), dv(wdt),
+                                torch.tensor([ws], device=cuda_dev), R, dv(z), dv(base), bsz, L, split=split,
+                                h_out=h)
+        assert np.array_equal(y.cpu().numpy().view(np.uint32), y_ref.view(np.uint32)), split
+        assert np.array_equal(h.cpu().numpy().view(np.uint32), h_ref.view(np.uint32)), split
+
+
+def test_argmax_rows_ties_nan_and_inf(cuda_dev):
+    from mamba_integer_b200 import kernels
+    x = torch.randn(6, 1000)
+    x[0, 17] = x[0, 900] = 50.0            # tie: first index
+    x[1, :] = -float("inf")                 # all -inf: index 0
+    x[2, 5] = float("nan")                  # NaN counts as the maximum
+    x[2, 7] = float("nan")
+    x[3, 999] = float("inf")
+    x[4, :] = 0.0
+    x[4, 3] = -0.0                          # -0 == +0: still index 0
+    got = kernels.argmax_rows(x.to(cuda_dev)).cpu()
+    assert got.tolist() == torch.argmax(x, dim=-1).tolist() == [17, 0, 5, 999, 0, got[5].item()]
+    assert got[5].item() == int(torch.argmax(x[5]))
