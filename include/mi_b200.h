@@ -50,7 +50,7 @@ int mi_device_error(int* out, int clear, void* stream);
  * of y32 / y64 is non-NULL.  Preconditions checked on the device (error word
  * MI_DEV_PRECOND): 0 <= n <= 2^k; |x|, |B|, |C| <= 32767.  A state that
  * leaves int32, or a y32 value that does, sets MI_DEV_OVERFLOW.
- * Supports N = 16; 1 <= k <= 30.
+ * Supports N = 16; 1 <= k <= 30; D % 4 == 0; every pointer 16-byte aligned.
  * Replaces: launch_dyadic_scan, src/cuda_kernels/dyadic_mamba_kernel.cu:135-153
  * (state update :53-59), extended with the B/C terms of the selective scan.
  */

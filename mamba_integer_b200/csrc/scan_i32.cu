@@ -8,13 +8,19 @@
 // right shift, add) with the selective-scan input term B_t*x_t and the output
 // contraction C_t.h_t added.
 //
-// Layout / parallelism: one warp per CTA owns 16 channels of one sequence;
-// two lanes per channel each hold 8 of the 16 int32 states in registers for
-// the whole sequence (the recurrence is sequential in t).  x and B|C arrive
-// through a per-warp double-buffered cp.async ring of TC-step chunks (no
-// block-level barriers); the two half sums of y meet with one shuffle, y is
-// staged in shared memory and written as 16-byte vectors.  n stays in
-// registers.
+// Layout / parallelism: one warp per CTA owns 32/LPC channels of one
+// sequence; LPC lanes per channel each hold 16/LPC of the 16 int32 states in
+// registers for the whole sequence (the recurrence is sequential in t, so the
+// independent (sequence, channel, state) chains are all the parallelism there
+// is).  x and B|C arrive through a per-warp 4-deep cp.async ring of TC-step
+// chunks (three chunks in flight ahead of the one in use, no block-level
+// barriers).  Each lane folds its states' C*h into y with 64-bit
+// multiply-adds, the LPC partial sums meet in shuffles, y is staged in shared
+// memory and written as 16-byte vectors.  n stays in registers.  LPC = 2 at
+// config 2 sizes: the B|C values every lane must receive each step (a 16-byte
+// shared load delivers 512 bytes per warp) and the y shuffles share one
+// load/store data path, which fewer lanes per channel use less of per state
+// update.
 //
 // Exactness: the shifted product fits int32 whenever 0 <= n <= 2^k (so the
 // 64-bit shift result is truncated losslessly); |B*x| < 2^30 when
@@ -26,12 +32,19 @@
 namespace mi {
 namespace scan_i32 {
 
-constexpr int CH = 16;       // channels per warp
-constexpr int THREADS = 32;  // two lanes per channel
-constexpr int TC = 16;       // time steps per staged chunk
 constexpr int NS = 16;       // d_state
-constexpr int HALF = NS / 2;
+constexpr int THREADS = 32;
+constexpr int TC = 16;       // time steps per staged chunk
+constexpr int SST = 4;       // chunks in the ring (SST - 1 in flight ahead)
 
+template <int LPC>
+struct Geo {
+    static constexpr int SPL = NS / LPC;  // states per lane
+    static constexpr int CH = 32 / LPC;   // channels per warp
+    static constexpr int XQ = CH / 4;     // 16-byte chunks per staged x row
+};
+
+template <int CH>
 struct Stage {
     int32_t x[TC][CH];
     int32_t bc[TC][2 * NS];  // B[0..15] | C[0..15]
@@ -44,13 +57,15 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pr
 }
 
 // Stage chunk [t0, t0+TC) of x[b, :, d0:d0+CH] and B|C[b, :, :].
-__device__ __forceinline__ void load_chunk(Stage& st, int t0, const int32_t* __restrict__ x,
+template <int CH>
+__device__ __forceinline__ void load_chunk(Stage<CH>& st, int t0, const int32_t* __restrict__ x,
                                            const int32_t* __restrict__ Bm, const int32_t* __restrict__ Cm,
                                            size_t row0, int d0, int L, int D) {
+    constexpr int XQ = CH / 4;
     const int lane = threadIdx.x;
 #pragma unroll
-    for (int i = lane; i < TC * (CH / 4); i += 32) {  // x: TC rows x 4 chunks
-        const int r = i >> 2, q = i & 3;
+    for (int i = lane; i < TC * XQ; i += 32) {
+        const int r = i / XQ, q = i % XQ;
         const int t = t0 + r;
         const bool ok = (t < L) && (d0 + 4 * q < D);
         const int32_t* src = ok ? x + (row0 + t) * D + d0 + 4 * q : x;
@@ -67,28 +82,36 @@ __device__ __forceinline__ void load_chunk(Stage& st, int t0, const int32_t* __r
     }
 }
 
-template <bool Y64>
+__device__ __forceinline__ int out_of_range4(int4 v) {
+    // |v| > 32767 for any component (the preconditions of the exact int32 path)
+    return ((unsigned)v.x + 32767u > 65534u) | ((unsigned)v.y + 32767u > 65534u) |
+           ((unsigned)v.z + 32767u > 65534u) | ((unsigned)v.w + 32767u > 65534u);
+}
+
+template <int LPC, bool Y64>
 __global__ void __launch_bounds__(THREADS)
 scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, const int32_t* __restrict__ Cm,
                 const int32_t* __restrict__ n, int k, int32_t* __restrict__ y32, int64_t* __restrict__ y64,
                 int32_t* __restrict__ h_io, int L, int D) {
-    __shared__ __align__(16) Stage stage[2];
+    using G = Geo<LPC>;
+    constexpr int SPL = G::SPL, CH = G::CH;
+    __shared__ __align__(16) Stage<CH> stage[SST];
     __shared__ __align__(16) int64_t ys[TC][CH];
     const int lane = threadIdx.x;
     const int b = blockIdx.y;
     const int d0 = blockIdx.x * CH;
-    const int ch = lane >> 1;   // channel within the warp
-    const int half = lane & 1;  // which 8 states
+    const int ch = lane / LPC;   // channel within the warp
+    const int sub = lane % LPC;  // which SPL states
     const int d = d0 + ch;
     const bool active = d < D;
     const size_t row0 = (size_t)b * L;
 
-    int32_t h[HALF], nn[HALF];
+    int32_t h[SPL], nn[SPL];
     int bad = 0;
     const int32_t lim = 1 << k;
 #pragma unroll
-    for (int j = 0; j < HALF; j++) {
-        const int jj = half * HALF + j;
+    for (int j = 0; j < SPL; j++) {
+        const int jj = sub * SPL + j;
         h[j] = active ? h_io[((size_t)b * D + d) * NS + jj] : 0;
         nn[j] = active ? n[(size_t)d * NS + jj] : 0;
         bad |= (nn[j] < 0) | (nn[j] > lim);
@@ -96,60 +119,65 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
 
     int ovf = 0;  // sign-test accumulator: negative => an int32 state or y32 overflowed
     const int nchunks = cdiv(L, TC);
-    load_chunk(stage[0], 0, x, Bm, Cm, row0, d0, L, D);
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-    for (int c = 0; c < nchunks; c++) {
-        Stage& st = stage[c & 1];
-        if (c + 1 < nchunks) load_chunk(stage[(c + 1) & 1], (c + 1) * TC, x, Bm, Cm, row0, d0, L, D);
+#pragma unroll
+    for (int c = 0; c < SST - 1; c++) {
+        if (c < nchunks) load_chunk<CH>(stage[c], c * TC, x, Bm, Cm, row0, d0, L, D);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
-        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    }
+    for (int c = 0; c < nchunks; c++) {
+        Stage<CH>& st = stage[c % SST];
+        // the slot refilled here was emptied by the previous iteration
+        if (c + SST - 1 < nchunks)
+            load_chunk<CH>(stage[(c + SST - 1) % SST], (c + SST - 1) * TC, x, Bm, Cm, row0, d0, L, D);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(SST - 1) : "memory");
         __syncwarp();
-        // range check of the staged inputs: 24 values per lane per chunk
+        // range check of the staged inputs
 #pragma unroll
-        for (int i = lane; i < TC * CH; i += 32) {
-            const int32_t v = (&st.x[0][0])[i];
-            bad |= (v < -32767) | (v > 32767);
-        }
+        for (int i = lane; i < TC * CH / 4; i += 32) bad |= out_of_range4(reinterpret_cast<const int4*>(&st.x[0][0])[i]);
 #pragma unroll
-        for (int i = lane; i < TC * 2 * NS; i += 32) {
-            const int32_t v = (&st.bc[0][0])[i];
-            bad |= (v < -32767) | (v > 32767);
-        }
+        for (int i = lane; i < TC * 2 * NS / 4; i += 32)
+            bad |= out_of_range4(reinterpret_cast<const int4*>(&st.bc[0][0])[i]);
         const int t0 = c * TC;
         const int tn = min(TC, L - t0);
 #pragma unroll 2
         for (int r = 0; r < tn; r++) {
             const int32_t xv = st.x[r][ch];
-            const int4 b0 = *reinterpret_cast<const int4*>(&st.bc[r][half * HALF]);
-            const int4 b1 = *reinterpret_cast<const int4*>(&st.bc[r][half * HALF + 4]);
-            const int4 c0 = *reinterpret_cast<const int4*>(&st.bc[r][NS + half * HALF]);
-            const int4 c1 = *reinterpret_cast<const int4*>(&st.bc[r][NS + half * HALF + 4]);
-            const int32_t bb[HALF] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-            const int32_t cc[HALF] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-            // the 8 state chains are independent; the integer sums below are exact
-            // in any order, so they are formed as trees to keep dependency chains short
-            long long prod[HALF];
-            int32_t ov[HALF];
+            int32_t bb[SPL], cc[SPL];
 #pragma unroll
-            for (int j = 0; j < HALF; j++) {
+            for (int q = 0; q < SPL / 4; q++) {
+                const int4 b4 = *reinterpret_cast<const int4*>(&st.bc[r][sub * SPL + 4 * q]);
+                const int4 c4 = *reinterpret_cast<const int4*>(&st.bc[r][NS + sub * SPL + 4 * q]);
+                bb[4 * q] = b4.x; bb[4 * q + 1] = b4.y; bb[4 * q + 2] = b4.z; bb[4 * q + 3] = b4.w;
+                cc[4 * q] = c4.x; cc[4 * q + 1] = c4.y; cc[4 * q + 2] = c4.z; cc[4 * q + 3] = c4.w;
+            }
+            // two independent 64-bit multiply-add chains for y (integer sums are
+            // exact in any order)
+            long long acc0 = 0, acc1 = 0;
+            int32_t ovl = 0;
+#pragma unroll
+            for (int j = 0; j < SPL; j++) {
                 const long long p = (long long)h[j] * (long long)nn[j];
                 const int32_t s = (int32_t)(p >> k);
                 const int32_t bx = (int32_t)((uint32_t)bb[j] * (uint32_t)xv);  // |B*x| < 2^30 when in range
                 const int32_t hn = (int32_t)((uint32_t)s + (uint32_t)bx);
-                ov[j] = (s ^ hn) & (bx ^ hn);
+                ovl |= (s ^ hn) & (bx ^ hn);
                 h[j] = hn;
-                prod[j] = (long long)cc[j] * (long long)hn;
+                if (j & 1) acc1 += (long long)cc[j] * (long long)hn;
+                else acc0 += (long long)cc[j] * (long long)hn;
             }
-            ovf |= ((ov[0] | ov[1]) | (ov[2] | ov[3])) | ((ov[4] | ov[5]) | (ov[6] | ov[7]));
-            long long acc = ((prod[0] + prod[1]) + (prod[2] + prod[3])) + ((prod[4] + prod[5]) + (prod[6] + prod[7]));
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            if (half == 0) ys[r][ch] = acc;
+            ovf |= ovl;
+            long long acc = acc0 + acc1;
+#pragma unroll
+            for (int o = 1; o < LPC; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+            if (sub == 0) ys[r][ch] = acc;
         }
         __syncwarp();
         // write the chunk's y rows: TC rows x CH values as 16-byte vectors
         if (Y64) {
+#pragma unroll
             for (int i = lane; i < TC * (CH / 2); i += 32) {
-                const int r = i >> 3, q = i & 7;  // 8 chunks of two int64 per row
+                const int r = i / (CH / 2), q = i % (CH / 2);  // chunks of two int64 per row
                 const int dq = d0 + 2 * q;
                 if (r < tn && dq < D) {
                     int64_t* o = y64 + (row0 + t0 + r) * D + dq;
@@ -157,8 +185,9 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
                 }
             }
         } else {
+#pragma unroll
             for (int i = lane; i < TC * (CH / 4); i += 32) {
-                const int r = i >> 2, q = i & 3;  // 4 chunks of four int32 per row
+                const int r = i / (CH / 4), q = i % (CH / 4);  // chunks of four int32 per row
                 const int dq = d0 + 4 * q;
                 if (r < tn && dq < D) {
                     int32_t v[4];
@@ -172,16 +201,27 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
                 }
             }
         }
-        __syncwarp();  // ys and the stage buffer are rewritten next iteration
+        __syncwarp();  // ys and the stage slot are rewritten in the next iterations
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 
     if (active) {
+        int4* hp = reinterpret_cast<int4*>(h_io + ((size_t)b * D + d) * NS + sub * SPL);
 #pragma unroll
-        for (int j = 0; j < HALF; j++) h_io[((size_t)b * D + d) * NS + half * HALF + j] = h[j];
+        for (int q = 0; q < SPL / 4; q++) hp[q] = make_int4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
     }
     if (ovf < 0) raise_dev_error(MI_DEV_OVERFLOW);
     if (bad) raise_dev_error(MI_DEV_PRECOND);
+}
+
+template <int LPC>
+static void launch_scan_i32(const int32_t* x, const int32_t* B, const int32_t* C, const int32_t* n, int k,
+                            int32_t* y32, int64_t* y64, int32_t* h_io, int batch, int L, int D, cudaStream_t s) {
+    dim3 grid(cdiv(D, Geo<LPC>::CH), batch);
+    if (y64)
+        scan_i32_kernel<LPC, true><<<grid, THREADS, 0, s>>>(x, B, C, n, k, nullptr, y64, h_io, L, D);
+    else
+        scan_i32_kernel<LPC, false><<<grid, THREADS, 0, s>>>(x, B, C, n, k, y32, nullptr, h_io, L, D);
 }
 
 }  // namespace scan_i32
@@ -191,20 +231,22 @@ extern "C" int mi_scan_i32(const int32_t* x, const int32_t* B, const int32_t* C,
                            int32_t* y32, int64_t* y64, int32_t* h_io, int batch, int L, int D, int N,
                            void* stream) {
     using namespace mi::scan_i32;
+    using mi::cdiv;
     if (!x || !B || !C || !n || !h_io) return MI_ERR_INVALID;
     if ((y32 == nullptr) == (y64 == nullptr)) return MI_ERR_INVALID;
     if (batch <= 0 || L <= 0 || D <= 0) return MI_ERR_INVALID;
     if (N != NS) return MI_ERR_UNSUPPORTED;
     if (k < 1 || k > 30) return MI_ERR_UNSUPPORTED;
     if (D % 4 != 0) return MI_ERR_UNSUPPORTED;  // 16-byte staging of x rows and vector y stores
-    if (((uintptr_t)x | (uintptr_t)B | (uintptr_t)C | (uintptr_t)y32 | (uintptr_t)y64) & 15) return MI_ERR_INVALID;
+    if (((uintptr_t)x | (uintptr_t)B | (uintptr_t)C | (uintptr_t)y32 | (uintptr_t)y64 | (uintptr_t)h_io) & 15)
+        return MI_ERR_INVALID;
     if (batch > 65535) return MI_ERR_UNSUPPORTED;
-    dim3 grid(mi::cdiv(D, CH), batch);
     cudaStream_t s = (cudaStream_t)stream;
-    if (y64)
-        scan_i32_kernel<true><<<grid, THREADS, 0, s>>>(x, B, C, n, k, nullptr, y64, h_io, L, D);
+    // 2 lanes per channel; 4 when the batch leaves too few warps to fill the GPU
+    if ((long long)batch * cdiv(D, Geo<2>::CH) >= 4LL * 148)
+        launch_scan_i32<2>(x, B, C, n, k, y32, y64, h_io, batch, L, D, s);
     else
-        scan_i32_kernel<false><<<grid, THREADS, 0, s>>>(x, B, C, n, k, y32, nullptr, h_io, L, D);
+        launch_scan_i32<4>(x, B, C, n, k, y32, y64, h_io, batch, L, D, s);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

@@ -28,7 +28,7 @@ def _eq(a, b, what=""):
 
 
 # ---------------------------------------------------------------- integer scan
-@pytest.mark.parametrize("bsz,L,D", [(2, 300, 200), (1, 33, 64), (3, 1, 4), (2, 4096, 128)])
+@pytest.mark.parametrize("bsz,L,D", [(2, 300, 200), (1, 33, 64), (3, 1, 4), (2, 4096, 128), (4, 37, 2400)])
 def test_scan_i32_matches_oracle(cuda_dev, bsz, L, D):
     k = _mi()
     g = torch.Generator().manual_seed(bsz * 1000 + L + D)
@@ -46,6 +46,23 @@ def test_scan_i32_matches_oracle(cuda_dev, bsz, L, D):
         y32, h32 = k.scan_i32(*dv[:4], 15, h0=dv[4], y_dtype=torch.int32)
         _eq(y32, y_ref.astype(np.int32), "y32")
         _eq(h32, h_ref, "h32")
+
+
+@pytest.mark.parametrize("bsz,D", [(4, 2400), (1, 64)])  # 2 and 4 lanes per channel
+def test_scan_i32_full_input_range(cuda_dev, bsz, D):
+    """B and C over the whole stated range +-32767 (the kernel repacks them as 16-bit pairs)."""
+    k = _mi()
+    L = 50
+    g = torch.Generator().manual_seed(D + bsz)
+    B = torch.randint(-32767, 32768, (bsz, L, 16), generator=g, dtype=torch.int32)
+    C = torch.randint(-32767, 32768, (bsz, L, 16), generator=g, dtype=torch.int32)
+    B[0, 0, :2], C[0, 0, :2] = torch.tensor([32767, -32767]), torch.tensor([-32767, 32767])
+    x = torch.randint(-3, 4, (bsz, L, D), generator=g, dtype=torch.int32)
+    n = torch.randint(0, 32769, (D, 16), generator=g, dtype=torch.int32)
+    y_ref, h_ref = orc.scan_i32(x.numpy(), B.numpy(), C.numpy(), n.numpy(), 15)
+    y64, h64 = k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), 15, y_dtype=torch.int64)
+    _eq(y64, y_ref, "y64")
+    _eq(h64, h_ref, "h")
 
 
 def test_scan_i32_kat_negative_floor(cuda_dev):
