@@ -277,7 +277,7 @@ def decode_metrics(dev, steps: int = 64, warmup: int = 3, batch: int | None = No
     return {"config": f"config5: 24L d1024, {B} streams, 512-token prompt, greedy steps", "steps_timed": steps,
             "ms_per_step": ms, "tok_per_s": B / ms * 1e3, "hbm_bytes_per_step": nbytes,
             "achieved_GB_per_s": nbytes / ms / 1e6, "hbm_frac": nbytes / ms / 1e6 / hbm, "peak_source": src,
-            "launches_per_step": DecodeEngine.launches_per_step(L), "cuda_graph": True}
+            "launches_per_step": eng.launches_per_step(), "cuda_graph": True}
 
 
 def cpu_baseline(n_tokens: int = 256, threads: int = 0):

@@ -156,6 +156,17 @@ int mi_conv_act_quant(const float* xz, int ldx, const float* w, const float* bia
                       int8_t* xq, float* xscale, float* amax_ws, int batch, int L, int D, void* stream);
 
 /*
+ * mi_conv_act_quant in one kernel and without a workspace: each CTA owns whole
+ * rows (D/4 threads, 4 channels each) for a chunk of positions, reduces the
+ * row absmax in the block and quantises from registers.  Same results as
+ * mi_conv_act_quant.  D % 4 == 0, D <= 4096; xq required.
+ * Replaces: conv1d + fused_squareplus_clamp + activation_quant_dynamic,
+ * src/mamba_integer_model.py:404-411 (quantisation: src/rational_bitnet.py:102-111).
+ */
+int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, const float* bias, float* act,
+                           int8_t* xq, float* xscale, int batch, int L, int D, void* stream);
+
+/*
  * mi_conv_act_quant without the caller-provided workspace, for hosts that
  * cannot call cudaMalloc (a runtime whose device memory belongs to another
  * allocator, a serving loop that must not allocate).  No counterpart in the
@@ -235,6 +246,24 @@ int mi_conv_step(const float* xz, int ldx, const float* w, const float* bias, fl
 int mi_ssm_step(const float* act, const float* xp, int ldxp, int R, const int8_t* w_dt,
                 const float* w_dt_scale, const float* z, int ldz, const float* base, float* h, float* y,
                 int8_t* xq, float* xscale, int batch, int D, int N, void* stream);
+
+/*
+ * mi_decode_mid: mi_conv_step, the x_proj BitLinear and mi_ssm_step in one
+ * kernel (one CTA per stream): everything between a layer's in_proj and
+ * out_proj GEMMs for one decode position.  xz [batch, ldx] = [x (D) | z (D)]
+ * (the in_proj output); win [batch, 3, D] and h [batch, D, N] advanced in
+ * place; w_x int8 [R + 2N, D] with its scale w_x_scale [1] (x_proj as exact
+ * int32 dot products, rescaled as the GEMM epilogue does); w_dt int8
+ * [D, R16], base [D, N]; xp_out (optional) [batch, R + 2N] receives the
+ * x_proj output; xq [batch, D] / xscale [batch]: y quantised for out_proj.
+ * N == 16, D % 16 == 0, D <= 4096, R <= 64.
+ * Replaces: the conv .. gate section of MambaIntegerBlock.forward at the last
+ * position, src/mamba_integer_model.py:404-444.
+ */
+int mi_decode_mid(const float* xz, int ldx, const float* conv_w, const float* conv_b, float* win,
+                  const int8_t* w_x, const float* w_x_scale, int R, const int8_t* w_dt,
+                  const float* w_dt_scale, const float* base, float* h, float* xp_out, int8_t* xq,
+                  float* xscale, int batch, int D, int N, void* stream);
 
 /*
  * mi_argmax_rows: out[t] = torch.argmax(x[t, :V]) (first index of the

@@ -37,10 +37,12 @@ SIGNATURES = {
     "mi_bitlinear_packed": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_conv_act_quant_noalloc": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
+    "mi_conv_act_quant_rows": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_ssm_scan": [_p, _p, _i, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
     "mi_ssm_scan_dt": [_p, _p, _i, _p, _i, _p, _p, _p, _i, _p, _i, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_conv_step": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mi_ssm_step": [_p, _p, _i, _i, _p, _p, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
+    "mi_decode_mid": [_p, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_argmax_rows": [_p, _i, _i, _i, _p, _p],
     "mi_scan_convex": [_p, _p, _p, _i, _i, _i, _p],
     "mi_squareplus_clamp": [_p, _p, _i64, _f, _f, _p],

@@ -6,6 +6,9 @@
 //     dt_proj dot products, decay / dt / u, one convex dyadic update of the
 //     16 fp32 states per channel (kept per stream in HBM), y = sum_n h*C, the
 //     gate and the int8 quantisation of y;
+//   * decode_mid_kernel: the two above with the x_proj BitLinear between them
+//     (int8 dot products by dp4a) in one kernel: everything between the
+//     in_proj and out_proj GEMMs of a layer;
 //   * argmax_rows_kernel: greedy token choice over the logits.
 // One CTA per stream: a stream's row never leaves its CTA, so the row absmax
 // of each quantisation is a block reduction instead of an atomic.
@@ -28,13 +31,7 @@ constexpr int CONV_CHUNKS = MAX_D / 4 / STEP_THREADS;   // float4 chunks per thr
 constexpr int SSM_CH = MAX_D / STEP_THREADS;            // channels per thread
 constexpr int MAX_R16 = 64;                             // dt_rank padded to 16
 
-// activation_quant_dynamic's scale (src/rational_bitnet.py:102-111), as the
-// row kernels compute it: s = max(amax, 1e-8), inv = reciprocal(s) * 127.
-__device__ __forceinline__ float quant_inv(float amax, float& xscale) {
-    const float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
-    xscale = __fdiv_rn(sc, 127.0f);
-    return __fmul_rn(__frcp_rn(sc), 127.0f);
-}
+__device__ __forceinline__ float quant_inv(float amax, float& xscale) { return quant_inv_scale(amax, xscale); }
 
 // Block-wide max of non-negative fp32 bit patterns (NaN sorts above +inf).
 __device__ __forceinline__ unsigned block_max_u32(unsigned m, unsigned* red) {
@@ -47,6 +44,48 @@ __device__ __forceinline__ unsigned block_max_u32(unsigned m, unsigned* red) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
     return m;
+}
+
+// Conv at the newest position for channels c..c+3 of one stream: wrow holds
+// the window rows x_{t-3}, x_{t-2}, x_{t-1} (row pitch D), x_t comes from
+// xrow; returns squareplus(ste_clamp(conv, +-50)) and advances the window.
+__device__ __forceinline__ float4 conv_chunk_step(const float* __restrict__ xrow, float* __restrict__ wrow,
+                                                  const float* __restrict__ w, const float* __restrict__ bias, int c,
+                                                  int D) {
+    const float4 x0 = *reinterpret_cast<const float4*>(wrow + c);
+    const float4 x1 = *reinterpret_cast<const float4*>(wrow + D + c);
+    const float4 x2 = *reinterpret_cast<const float4*>(wrow + 2 * D + c);
+    const float4 x3 = *reinterpret_cast<const float4*>(xrow + c);
+    const float4 bs = *reinterpret_cast<const float4*>(bias + c);
+    const float xs0[4] = {x0.x, x0.y, x0.z, x0.w}, xs1[4] = {x1.x, x1.y, x1.z, x1.w};
+    const float xs2[4] = {x2.x, x2.y, x2.z, x2.w}, xs3[4] = {x3.x, x3.y, x3.z, x3.w};
+    const float bv[4] = {bs.x, bs.y, bs.z, bs.w};
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        const float4 wc = *reinterpret_cast<const float4*>(w + 4 * (c + e));
+        // bias first, then one FMA per tap k = 0..3 over positions t-3+k
+        float acc = bv[e];
+        acc = __fmaf_rn(wc.x, xs0[e], acc);
+        acc = __fmaf_rn(wc.y, xs1[e], acc);
+        acc = __fmaf_rn(wc.z, xs2[e], acc);
+        acc = __fmaf_rn(wc.w, xs3[e], acc);
+        r[e] = squareplus_bounded(ste_clamp(acc, -50.0f, 50.0f));
+    }
+    *reinterpret_cast<float4*>(wrow + c) = x1;
+    *reinterpret_cast<float4*>(wrow + D + c) = x2;
+    *reinterpret_cast<float4*>(wrow + 2 * D + c) = x3;
+    return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+__device__ __forceinline__ unsigned absmax_bits4(float4 v) {
+    return max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+               max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+}
+
+__device__ __forceinline__ char4 quant4(float4 v, float inv) {
+    return make_char4((signed char)quant_i8(__fmul_rn(v.x, inv)), (signed char)quant_i8(__fmul_rn(v.y, inv)),
+                      (signed char)quant_i8(__fmul_rn(v.z, inv)), (signed char)quant_i8(__fmul_rn(v.w, inv)));
 }
 
 // xz row b: the first D columns are the conv input x_t; win [batch, 3, D]:
@@ -65,32 +104,8 @@ conv_step_kernel(const float* __restrict__ xz, int ldx, const float* __restrict_
     for (int i = 0; i < CONV_CHUNKS; i++) {
         const int c = 4 * (threadIdx.x + i * STEP_THREADS);
         if (c < D) {
-            const float4 x0 = *reinterpret_cast<const float4*>(wrow + c);
-            const float4 x1 = *reinterpret_cast<const float4*>(wrow + D + c);
-            const float4 x2 = *reinterpret_cast<const float4*>(wrow + 2 * D + c);
-            const float4 x3 = *reinterpret_cast<const float4*>(xrow + c);
-            const float4 bs = *reinterpret_cast<const float4*>(bias + c);
-            float r[4];
-            const float xs0[4] = {x0.x, x0.y, x0.z, x0.w}, xs1[4] = {x1.x, x1.y, x1.z, x1.w};
-            const float xs2[4] = {x2.x, x2.y, x2.z, x2.w}, xs3[4] = {x3.x, x3.y, x3.z, x3.w};
-            const float bv[4] = {bs.x, bs.y, bs.z, bs.w};
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const float4 wc = *reinterpret_cast<const float4*>(w + 4 * (c + e));
-                // bias first, then one FMA per tap k = 0..3 over positions t-3+k
-                float acc = bv[e];
-                acc = __fmaf_rn(wc.x, xs0[e], acc);
-                acc = __fmaf_rn(wc.y, xs1[e], acc);
-                acc = __fmaf_rn(wc.z, xs2[e], acc);
-                acc = __fmaf_rn(wc.w, xs3[e], acc);
-                r[e] = squareplus_bounded(ste_clamp(acc, -50.0f, 50.0f));
-                m = max(m, __float_as_uint(fabsf(r[e])));
-            }
-            a[i] = make_float4(r[0], r[1], r[2], r[3]);
-            // advance the window
-            *reinterpret_cast<float4*>(wrow + c) = x1;
-            *reinterpret_cast<float4*>(wrow + D + c) = x2;
-            *reinterpret_cast<float4*>(wrow + 2 * D + c) = x3;
+            a[i] = conv_chunk_step(xrow, wrow, w, bias, c, D);
+            m = max(m, absmax_bits4(a[i]));
             if (act) *reinterpret_cast<float4*>(act + (size_t)b * D + c) = a[i];
         }
     }
@@ -100,15 +115,75 @@ conv_step_kernel(const float* __restrict__ xz, int ldx, const float* __restrict_
 #pragma unroll
     for (int i = 0; i < CONV_CHUNKS; i++) {
         const int c = 4 * (threadIdx.x + i * STEP_THREADS);
-        if (c < D) {
-            const char4 q = make_char4((signed char)quant_i8(__fmul_rn(a[i].x, inv)),
-                                       (signed char)quant_i8(__fmul_rn(a[i].y, inv)),
-                                       (signed char)quant_i8(__fmul_rn(a[i].z, inv)),
-                                       (signed char)quant_i8(__fmul_rn(a[i].w, inv)));
-            *reinterpret_cast<char4*>(xq + (size_t)b * D + c) = q;
-        }
+        if (c < D) *reinterpret_cast<char4*>(xq + (size_t)b * D + c) = quant4(a[i], inv);
     }
     if (threadIdx.x == 0) xscale[b] = xs;
+}
+
+// activation_quant_dynamic of the dt row (R values of `row`), as
+// mi_quantize_rows computes it, by one full warp: int8 values into dtq (R16
+// bytes, zero-padded), the scale into *dts.
+__device__ __forceinline__ void dt_row_quant(const float* row, int R, int R16, int32_t* dtq, float* dts) {
+    const int lane = threadIdx.x & 31;
+    float am = 0.0f;
+    bool nan = false;
+    for (int k = lane; k < R; k += 32) {
+        const float v = fabsf(row[k]);
+        nan |= (v != v);
+        am = fmaxf(am, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    nan = __any_sync(0xffffffffu, nan);
+    const float amax = nan ? __int_as_float(0x7fc00000) : am;
+    float xs;
+    const float inv = quant_inv(amax, xs);
+    int8_t* q8 = reinterpret_cast<int8_t*>(dtq);
+    for (int k = lane; k < R16; k += 32) q8[k] = k < R ? (int8_t)quant_i8(__fmul_rn(row[k], inv)) : (int8_t)0;
+    if (lane == 0) *dts = xs;
+}
+
+// One channel c of the scan step: dt_proj (exact int32 dot product of the
+// quantised dt row with w_dt row c, then the BitLinear rescale), decay / dt /
+// u, the convex update of its 16 states in hrow (in place), y = sum h*C and
+// the gate with zv.  bc = B (16) | C (16).
+__device__ __forceinline__ float ssm_channel_step(int c, float actv, float zv, const int32_t* dtq, int R16,
+                                                  const int8_t* __restrict__ w_dt, float dscale,
+                                                  const float* __restrict__ base, float* hrow, const float* bc) {
+    constexpr int NS = 16;
+    const int4* wq = reinterpret_cast<const int4*>(w_dt + (size_t)c * R16);
+    int acc = 0;
+    for (int k = 0; k < R16 / 16; k++) {
+        const int4 wv = wq[k];
+        acc = __dp4a(dtq[4 * k], wv.x, acc);
+        acc = __dp4a(dtq[4 * k + 1], wv.y, acc);
+        acc = __dp4a(dtq[4 * k + 2], wv.z, acc);
+        acc = __dp4a(dtq[4 * k + 3], wv.w, acc);
+    }
+    const float mod = ste_clamp(__fmul_rn((float)acc, dscale), -20.0f, 20.0f);                   // (:419-421)
+    const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);          // (:425-427)
+    const float xdt = __fmul_rn(actv, dtv);
+    float4* hp = reinterpret_cast<float4*>(hrow);
+    const float4* bp = reinterpret_cast<const float4*>(base + (size_t)c * NS);
+    float yacc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NS / 4; q++) {
+        const float4 hv4 = hp[q], bv4 = bp[q];
+        float hv[4] = {hv4.x, hv4.y, hv4.z, hv4.w};
+        const float bv[4] = {bv4.x, bv4.y, bv4.z, bv4.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int n = 4 * q + e;
+            // decay_nums = ste_clamp(base + mod, 0, 32000); decay = nums / 2^15   (:423-424, :305)
+            const float num = ste_clamp(__fadd_rn(bv[e], mod), 0.0f, 32000.0f);
+            const float dec = __fmul_rn(num, 3.0517578125e-05f);
+            const float u = __fmul_rn(xdt, bc[n]);
+            hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));  // (:309)
+            yacc = __fmaf_rn(hv[e], bc[NS + n], yacc);                                 // (:440)
+        }
+        hp[q] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+    }
+    return sigmoid_gate(yacc, zv);                                                      // (:441-444)
 }
 
 // One step of the selective scan for stream b (blockIdx.x).
@@ -130,29 +205,11 @@ ssm_step_kernel(const float* __restrict__ act, const float* __restrict__ xp, int
     const float* row = xp + (size_t)b * ldxp;
     const int R16 = (R + 15) / 16 * 16;
     if (threadIdx.x < 32) {
-        // activation_quant_dynamic of the dt row, as mi_quantize_rows computes it
-        const int lane = threadIdx.x;
-        float am = 0.0f;
-        bool nan = false;
-        for (int k = lane; k < R; k += 32) {
-            const float v = fabsf(row[k]);
-            nan |= (v != v);
-            am = fmaxf(am, v);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-        nan = __any_sync(0xffffffffu, nan);
-        const float amax = nan ? __int_as_float(0x7fc00000) : am;
-        float xs;
-        const float inv = quant_inv(amax, xs);
-        int8_t* q8 = reinterpret_cast<int8_t*>(dtq_s);
-        for (int k = lane; k < R16; k += 32) q8[k] = k < R ? (int8_t)quant_i8(__fmul_rn(row[k], inv)) : (int8_t)0;
-        if (lane == 0) dts_s = xs;
-        bc_s[lane] = row[R + lane];  // B (16) then C (16)
+        dt_row_quant(row, R, R16, dtq_s, &dts_s);
+        bc_s[threadIdx.x] = row[R + threadIdx.x];  // B (16) then C (16)
     }
     __syncthreads();
-    const float wsc = *w_dt_scale;
-    const float dscale = __fmul_rn(wsc, dts_s);  // (w_scale * x_scale) of the dt_proj BitLinear
+    const float dscale = __fmul_rn(*w_dt_scale, dts_s);  // (w_scale * x_scale) of the dt_proj BitLinear
     float yv[SSM_CH];
     unsigned m = 0u;
 #pragma unroll
@@ -160,40 +217,8 @@ ssm_step_kernel(const float* __restrict__ act, const float* __restrict__ xp, int
         const int c = threadIdx.x + i * STEP_THREADS;
         yv[i] = 0.0f;
         if (c >= D) continue;
-        // dt_proj: exact int32 dot product, then the BitLinear rescale
-        const int4* wq = reinterpret_cast<const int4*>(w_dt + (size_t)c * R16);
-        int acc = 0;
-        for (int k = 0; k < R16 / 16; k++) {
-            const int4 wv = wq[k];
-            acc = __dp4a(dtq_s[4 * k], wv.x, acc);
-            acc = __dp4a(dtq_s[4 * k + 1], wv.y, acc);
-            acc = __dp4a(dtq_s[4 * k + 2], wv.z, acc);
-            acc = __dp4a(dtq_s[4 * k + 3], wv.w, acc);
-        }
-        const float mod = ste_clamp(__fmul_rn((float)acc, dscale), -20.0f, 20.0f);       // (:419-421)
-        const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);  // (:425-427)
-        const float xdt = __fmul_rn(act[(size_t)b * D + c], dtv);
-        float4* hp = reinterpret_cast<float4*>(h + ((size_t)b * D + c) * NS);
-        const float4* bp = reinterpret_cast<const float4*>(base + (size_t)c * NS);
-        float yacc = 0.0f;
-#pragma unroll
-        for (int q = 0; q < NS / 4; q++) {
-            const float4 hv4 = hp[q], bv4 = bp[q];
-            float hv[4] = {hv4.x, hv4.y, hv4.z, hv4.w};
-            const float bv[4] = {bv4.x, bv4.y, bv4.z, bv4.w};
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int n = 4 * q + e;
-                // decay_nums = ste_clamp(base + mod, 0, 32000); decay = nums / 2^15   (:423-424, :305)
-                const float num = ste_clamp(__fadd_rn(bv[e], mod), 0.0f, 32000.0f);
-                const float dec = __fmul_rn(num, 3.0517578125e-05f);
-                const float u = __fmul_rn(xdt, bc_s[n]);
-                hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));  // (:309)
-                yacc = __fmaf_rn(hv[e], bc_s[NS + n], yacc);                                 // (:440)
-            }
-            hp[q] = make_float4(hv[0], hv[1], hv[2], hv[3]);
-        }
-        yv[i] = sigmoid_gate(yacc, z[(size_t)b * ldz + c]);                                  // (:441-444)
+        yv[i] = ssm_channel_step(c, act[(size_t)b * D + c], z[(size_t)b * ldz + c], dtq_s, R16, w_dt, dscale, base,
+                                 h + ((size_t)b * D + c) * NS, bc_s);
         if (y) y[(size_t)b * D + c] = yv[i];
         m = max(m, __float_as_uint(fabsf(yv[i])));
     }
@@ -206,6 +231,131 @@ ssm_step_kernel(const float* __restrict__ act, const float* __restrict__ xp, int
         if (c < D) xq[(size_t)b * D + c] = (int8_t)quant_i8(__fmul_rn(yv[i], inv));
     }
     if (threadIdx.x == 0) xscale[b] = xs;
+}
+
+// Everything between the in_proj and out_proj GEMMs of one layer for stream
+// b: conv step + activation + int8 quantisation (kept in shared memory), the
+// x_proj BitLinear as exact int32 dot products (warp w takes outputs w, w+16,
+// ...; each lane 16-byte chunks of the row) with the GEMM epilogue's rescale,
+// the dt row quantisation, then the scan step and gate (one channel per
+// thread per pass, so the 64-byte state rows of a warp are contiguous) and
+// the quantisation of y.  w_x int8 [R+32, D];
+// xp_out (optional) [batch, R+32] receives the x_proj output.
+// D % 16 == 0, D <= MAX_D, R <= 64.
+constexpr int MAX_P = MAX_R16 + 32;  // x_proj outputs: dt_rank + 2 * d_state
+constexpr int MID_THREADS = 512;     // 16 warps: more state loads in flight per SM
+constexpr int MID_CONV = MAX_D / 4 / MID_THREADS;  // conv chunks of 4 channels per thread
+constexpr int MID_CH = MAX_D / MID_THREADS;        // scan channels per thread
+
+template <int NT>
+__device__ __forceinline__ unsigned block_max_bits(unsigned m, unsigned* red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = lane < NT / 32 ? red[lane] : 0u;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+    return m;
+}
+
+__global__ void __launch_bounds__(MID_THREADS, 2)
+decode_mid_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ cw, const float* __restrict__ cb,
+                  float* __restrict__ win, const int8_t* __restrict__ w_x, const float* __restrict__ w_x_scale,
+                  int R, const int8_t* __restrict__ w_dt, const float* __restrict__ w_dt_scale,
+                  const float* __restrict__ base, float* __restrict__ h, float* __restrict__ xp_out,
+                  int8_t* __restrict__ xq, float* __restrict__ xscale, int D) {
+    constexpr int NS = 16;
+    constexpr int NW = MID_THREADS / 32;
+    constexpr int XCH = MAX_D / 16 / 32;  // 16-byte chunks of the row per lane
+    __shared__ __align__(16) float act_s[MAX_D];
+    __shared__ __align__(16) int8_t xq_s[MAX_D];
+    __shared__ float xp_s[MAX_P];
+    __shared__ __align__(16) int32_t dtq_s[MAX_R16 / 4];
+    __shared__ float dts_s;
+    __shared__ unsigned red[NW];
+    __shared__ unsigned red2[NW];
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int P = R + 2 * NS;
+    const int R16 = (R + 15) / 16 * 16;
+    const float* xrow = xz + (size_t)b * ldx;
+    float* wrow = win + (size_t)b * 3 * D;
+
+    // (1) conv + activation on this thread's chunks of 4 channels (into shared memory)
+    float4 a[MID_CONV];
+    unsigned m = 0u;
+#pragma unroll
+    for (int i = 0; i < MID_CONV; i++) {
+        const int c = 4 * (threadIdx.x + i * MID_THREADS);
+        a[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c < D) {
+            a[i] = conv_chunk_step(xrow, wrow, cw, cb, c, D);
+            m = max(m, absmax_bits4(a[i]));
+            *reinterpret_cast<float4*>(act_s + c) = a[i];
+        }
+    }
+    // (2) its int8 quantisation, into shared memory
+    float xs_c;
+    const float inv_c = quant_inv(__uint_as_float(block_max_bits<MID_THREADS>(m, red)), xs_c);
+#pragma unroll
+    for (int i = 0; i < MID_CONV; i++) {
+        const int c = 4 * (threadIdx.x + i * MID_THREADS);
+        if (c < D) *reinterpret_cast<char4*>(xq_s + c) = quant4(a[i], inv_c);
+    }
+    __syncthreads();
+    // (3) x_proj: acc * (w_scale * x_scale), as the GEMM epilogue computes it
+    const int nch = D / 16;
+    const float sc_x = __fmul_rn(*w_x_scale, xs_c);
+    for (int o = warp; o < P; o += NW) {
+        const int4* wr = reinterpret_cast<const int4*>(w_x + (size_t)o * D);
+        int acc = 0;
+#pragma unroll
+        for (int i = 0; i < XCH; i++) {
+            const int j = lane + 32 * i;
+            if (j < nch) {
+                const int4 wv = wr[j];
+                const int4 xv = reinterpret_cast<const int4*>(xq_s)[j];
+                acc = __dp4a(xv.x, wv.x, acc);
+                acc = __dp4a(xv.y, wv.y, acc);
+                acc = __dp4a(xv.z, wv.z, acc);
+                acc = __dp4a(xv.w, wv.w, acc);
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        if (lane == 0) {
+            const float v = __fmul_rn((float)acc, sc_x);
+            xp_s[o] = v;
+            if (xp_out) xp_out[(size_t)b * P + o] = v;
+        }
+    }
+    __syncthreads();
+    // (4) the dt row's quantisation
+    if (warp == 0) dt_row_quant(xp_s, R, R16, dtq_s, &dts_s);
+    __syncthreads();
+    const float dscale = __fmul_rn(*w_dt_scale, dts_s);
+    // (5) scan step + gate, one channel per thread per pass (coalesced state
+    // rows); y replaces act in shared memory (same thread, same index);
+    // (6) quantisation of y
+    unsigned my = 0u;
+    for (int i = 0; i < MID_CH; i++) {
+        const int c = threadIdx.x + i * MID_THREADS;
+        if (c < D) {
+            const float yv = ssm_channel_step(c, act_s[c], xrow[D + c], dtq_s, R16, w_dt, dscale, base,
+                                              h + ((size_t)b * D + c) * NS, xp_s + R);
+            act_s[c] = yv;
+            my = max(my, __float_as_uint(fabsf(yv)));
+        }
+    }
+    float xs_y;
+    const float inv_y = quant_inv(__uint_as_float(block_max_bits<MID_THREADS>(my, red2)), xs_y);
+    for (int i = 0; i < MID_CH; i++) {
+        const int c = threadIdx.x + i * MID_THREADS;
+        if (c < D) xq[(size_t)b * D + c] = (int8_t)quant_i8(__fmul_rn(act_s[c], inv_y));
+    }
+    if (threadIdx.x == 0) xscale[b] = xs_y;
 }
 
 // torch.argmax over each row: the first index of the maximum, NaN above
@@ -289,6 +439,28 @@ extern "C" int mi_ssm_step(const float* act, const float* xp, int ldxp, int R, c
     if (((uintptr_t)h | (uintptr_t)base | (uintptr_t)w_dt) & 15) return MI_ERR_INVALID;
     ssm_step_kernel<<<batch, STEP_THREADS, 0, (cudaStream_t)stream>>>(act, xp, ldxp, R, w_dt, w_dt_scale, z, ldz, base,
                                                                      h, y, xq, xscale, D);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+extern "C" int mi_decode_mid(const float* xz, int ldx, const float* conv_w, const float* conv_b, float* win,
+                             const int8_t* w_x, const float* w_x_scale, int R, const int8_t* w_dt,
+                             const float* w_dt_scale, const float* base, float* h, float* xp_out, int8_t* xq,
+                             float* xscale, int batch, int D, int N, void* stream) {
+    using namespace mi::decode;
+    if (!xz || !conv_w || !conv_b || !win || !w_x || !w_x_scale || !w_dt || !w_dt_scale || !base || !h || !xq ||
+        !xscale)
+        return MI_ERR_INVALID;
+    if (N != 16) return MI_ERR_UNSUPPORTED;
+    if (batch <= 0 || D <= 0 || R <= 0 || ldx < 2 * D) return MI_ERR_INVALID;
+    if (D % 16 != 0 || D > MAX_D || (R + 15) / 16 * 16 > MAX_R16 || ldx % 4 != 0) return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)xz | (uintptr_t)conv_w | (uintptr_t)conv_b | (uintptr_t)win | (uintptr_t)w_x | (uintptr_t)h |
+         (uintptr_t)base | (uintptr_t)w_dt) & 15)
+        return MI_ERR_INVALID;
+    if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
+    decode_mid_kernel<<<batch, MID_THREADS, 0, (cudaStream_t)stream>>>(xz, ldx, conv_w, conv_b, win, w_x, w_x_scale,
+                                                                        R, w_dt, w_dt_scale, base, h, xp_out, xq,
+                                                                        xscale, D);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

@@ -888,9 +888,18 @@ static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_sca
         if (N <= 96) return launch<96, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
         return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     }
-    if (N % 256 == 0)
+    // the widest N tile that still gives every SM a tile (few-row GEMMs, e.g.
+    // decoding, get narrower tiles and more CTAs)
+    const int sms = sm_count();
+    const long long tm = cdiv(M, BM);
+    auto fills = [&](int bn) { return tm * cdiv(N, bn) >= sms; };
+    if (N % 256 == 0 && fills(256))
         return launch<256, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
-    return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+    if (fills(128))
+        return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+    if (fills(64))
+        return launch<64, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+    return launch<32, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
 }
 
 // Dense int8 ternary rows -> the 2-bit format (one thread per 16-weight word).

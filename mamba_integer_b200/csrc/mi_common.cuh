@@ -149,6 +149,15 @@ __device__ __forceinline__ float pow2_scale(float var) {
     return s;
 }
 
+// activation_quant_dynamic's scale (src/rational_bitnet.py:102-111) from a
+// row's max |x|: s = max(amax, 1e-8) (NaN propagates), xscale = s / 127, and
+// the multiplier 127 / s computed as Tensor.__rdiv__ does: reciprocal(s) * 127.
+__device__ __forceinline__ float quant_inv_scale(float amax, float& xscale) {
+    const float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
+    xscale = __fdiv_rn(sc, 127.0f);
+    return __fmul_rn(__frcp_rn(sc), 127.0f);
+}
+
 // int8 value of clamp(ste_round(v), -127, 127), ste_round(v) = v + (rne(v) - v)
 // (src/rational_bitnet.py:54-60, :109)
 __device__ __forceinline__ int quant_i8(float v) {

@@ -97,6 +97,95 @@ conv_act_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__
     }
 }
 
+// Row-owning variant with the quantisation fused: one CTA holds whole rows
+// (all D channels, 4 adjacent channels per thread) for a chunk of CONV_TC
+// positions of one sequence, so the absmax of each position's row is a block
+// reduction and the int8 quantisation follows from the registers -- no second
+// pass over act, no atomics, no workspace.  Same arithmetic as
+// conv_act_kernel followed by quant_rows_kernel.
+constexpr int CONVR_G = 4;  // positions per group (one block reduction each group)
+
+__global__ void __launch_bounds__(1024)
+conv_rows_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w, const float* __restrict__ bias,
+                 float* __restrict__ act, int8_t* __restrict__ xq, float* __restrict__ xscale, int L, int D) {
+    __shared__ unsigned red[2][CONVR_G][32];  // per position: each warp's max |act| bits (double buffer)
+    const int c = 4 * threadIdx.x;  // first of this thread's 4 channels
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int b = blockIdx.y;
+    const int t0 = blockIdx.x * CONV_TC;
+    const bool active = c < D;
+    const int cc = active ? c : 0;
+    float4 wv[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) wv[e] = *reinterpret_cast<const float4*>(w + 4 * (cc + e));
+    const float4 bs = *reinterpret_cast<const float4*>(bias + cc);
+    const size_t row0 = (size_t)b * L;
+    const float* px = xz + row0 * ldx + cc;
+    const float4 zero4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    float4 w0 = (t0 - 3 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 3) * ldx) : zero4;
+    float4 w1 = (t0 - 2 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 2) * ldx) : zero4;
+    float4 w2 = (t0 - 1 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 1) * ldx) : zero4;
+    const int tend = min(L, t0 + CONV_TC);
+    int buf = 0;
+    for (int t = t0; t < tend; t += CONVR_G, buf ^= 1) {
+        float4 a[CONVR_G];
+#pragma unroll
+        for (int j = 0; j < CONVR_G; j++)
+            a[j] = (t + j < tend) ? __ldg(reinterpret_cast<const float4*>(px + (size_t)(t + j) * ldx)) : zero4;
+        unsigned m[CONVR_G];
+#pragma unroll
+        for (int j = 0; j < CONVR_G; j++) {
+            const float4 xv = a[j];
+            a[j].x = conv_tap4(bs.x, wv[0], w0.x, w1.x, w2.x, xv.x);
+            a[j].y = conv_tap4(bs.y, wv[1], w0.y, w1.y, w2.y, xv.y);
+            a[j].z = conv_tap4(bs.z, wv[2], w0.z, w1.z, w2.z, xv.z);
+            a[j].w = conv_tap4(bs.w, wv[3], w0.w, w1.w, w2.w, xv.w);
+            w0 = w1;
+            w1 = w2;
+            w2 = xv;
+            const bool ok = active && (t + j < tend);
+            if (ok) *reinterpret_cast<float4*>(act + (row0 + t + j) * D + c) = a[j];
+            const unsigned mx = max(max(__float_as_uint(fabsf(a[j].x)), __float_as_uint(fabsf(a[j].y))),
+                                    max(__float_as_uint(fabsf(a[j].z)), __float_as_uint(fabsf(a[j].w))));
+            m[j] = ok ? mx : 0u;  // fp32 bits of non-negative values order like unsigned ints, NaN on top
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int j = 0; j < CONVR_G; j++) m[j] = max(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
+        }
+        if (lane < CONVR_G) {
+            unsigned mine = 0u;
+#pragma unroll
+            for (int j = 0; j < CONVR_G; j++) mine = (lane == j) ? m[j] : mine;
+            red[buf][lane][warp] = mine;
+        }
+        // one barrier per group: every warp then reduces the per-warp maxima
+        // itself (lane j for position j); the buffers alternate, so the next
+        // group's writes cannot meet this group's reads
+        __syncthreads();
+        float inv_l = 0.0f;
+        if (lane < CONVR_G) {
+            unsigned mm = 0u;
+            for (int k = 0; k < nwarps; k++) mm = max(mm, red[buf][lane][k]);
+            float xs;
+            inv_l = quant_inv_scale(__uint_as_float(mm), xs);
+            if (warp == 0 && t + lane < tend) xscale[row0 + t + lane] = xs;
+        }
+#pragma unroll
+        for (int j = 0; j < CONVR_G; j++) {
+            const float inv = __shfl_sync(0xffffffffu, inv_l, j);
+            if (active && t + j < tend) {
+                const char4 q = make_char4((signed char)quant_i8(__fmul_rn(a[j].x, inv)),
+                                           (signed char)quant_i8(__fmul_rn(a[j].y, inv)),
+                                           (signed char)quant_i8(__fmul_rn(a[j].z, inv)),
+                                           (signed char)quant_i8(__fmul_rn(a[j].w, inv)));
+                *reinterpret_cast<char4*>(xq + (row0 + t + j) * D + c) = q;
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // fused selective scan
 // ---------------------------------------------------------------------------
@@ -665,6 +754,24 @@ extern "C" int mi_conv_act_quant(const float* xz, int ldx, const float* w, const
         xz, ldx, w, bias, act, reinterpret_cast<unsigned int*>(amax_ws), L, D);
     MI_CHECK_LAUNCH();
     if (xq) return mi_quantize_rows(act, D, T, D, xq, D, xscale, amax_ws, stream);
+    return MI_OK;
+}
+
+// mi_conv_act_quant with the row absmax and the quantisation inside the conv
+// kernel (one CTA per chunk of whole rows): no workspace, one launch.
+extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, const float* bias, float* act,
+                                      int8_t* xq, float* xscale, int batch, int L, int D, void* stream) {
+    if (!xz || !w || !bias || !act || !xq || !xscale) return MI_ERR_INVALID;
+    if (batch <= 0 || L <= 0 || D <= 0 || ldx < D) return MI_ERR_INVALID;
+    if (((uintptr_t)w | (uintptr_t)bias | (uintptr_t)xz | (uintptr_t)act) & 15) return MI_ERR_INVALID;
+    if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
+    if ((D | ldx) & 3) return MI_ERR_UNSUPPORTED;  // 16-byte vectors of 4 channels
+    if (D > 4096) return MI_ERR_UNSUPPORTED;       // D/4 threads per CTA
+    if (batch > 65535) return MI_ERR_UNSUPPORTED;
+    const int threads = mi::cdiv(D / 4, 32) * 32;
+    dim3 grid(mi::cdiv(L, mi::ssm::CONV_TC), batch);
+    mi::ssm::conv_rows_kernel<<<grid, threads, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale, L, D);
+    MI_CHECK_LAUNCH();
     return MI_OK;
 }
 

@@ -8,9 +8,9 @@ kernels over that cached state:
     rowprep      embedding gather (+ residual later) + BitShiftNorm + int8 quant  [B, d]
     per layer:
       in_proj    tcgen05 GEMM from 2-bit packed weights  -> xz        [B, 2di]
-      conv_step  conv window + ste_clamp + squareplus + int8 quant    [B, di]
-      x_proj     tcgen05 GEMM                            -> dt | B | C
-      ssm_step   dt quant + dt_proj + decay/dt/u + one state update + h.C + gate
+      mid        one kernel, one CTA per stream: conv window + ste_clamp +
+                 squareplus + int8 quant; x_proj as int8 dot products; dt
+                 quant + dt_proj + decay/dt/u + one state update + h.C + gate
                  + int8 quant                                          [B, di]
       out_proj   tcgen05 GEMM                            -> out       [B, d]
       rowprep    residual += out*res_gate, next norm + quant
@@ -78,10 +78,13 @@ class DecodeEngine:
     per token).  ``use_graph`` replays each step from a CUDA graph captured on
     the first step (the step launches no allocation and no host sync)."""
 
-    def __init__(self, model, prefill: PrefillEngine | None = None, use_graph: bool = True):
+    def __init__(self, model, prefill: PrefillEngine | None = None, use_graph: bool = True, fused: bool = True):
         self.pre = prefill if prefill is not None else PrefillEngine(model)
         self.n_layer = len(self.pre.layers)
         self.use_graph = use_graph
+        # fused: one mid kernel per layer (mi_decode_mid); otherwise conv step,
+        # x_proj GEMM and scan step as three launches
+        self.fused = fused and self.pre.di % 16 == 0
         self.states: StreamStates | None = None
         self.ws: _StepWorkspace | None = None
         self._graph = None
@@ -96,10 +99,14 @@ class DecodeEngine:
         kernels.rowprep(g0, s0, B, d, ids=ws.ids, emb=pre.emb, x_out=ws.x, xq=ws.xq_d, xscale=ws.xs_d)
         for i, p in enumerate(layers):
             ternary_matmul(ws.xq_d, p["w_in"], ws.xs_d, out=ws.xz)
-            kernels.conv_step(ws.xz, p["conv_w"], p["conv_b"], st.win[i], di, ws.xq_i, ws.xs_i, act=ws.act)
-            ternary_matmul(ws.xq_i, p["w_x"], ws.xs_i, out=ws.xp)
-            kernels.ssm_step(ws.act, ws.xp, R, p["w_dt"].w8, p["w_dt"].scale, ws.xz[:, di:], p["base"], st.h[i],
-                             ws.xq_i, ws.xs_i)
+            if self.fused:
+                kernels.decode_mid(ws.xz, p["conv_w"], p["conv_b"], st.win[i], p["w_x"].w8, p["w_x"].scale, R,
+                                   p["w_dt"].w8, p["w_dt"].scale, p["base"], st.h[i], ws.xq_i, ws.xs_i)
+            else:
+                kernels.conv_step(ws.xz, p["conv_w"], p["conv_b"], st.win[i], di, ws.xq_i, ws.xs_i, act=ws.act)
+                ternary_matmul(ws.xq_i, p["w_x"], ws.xs_i, out=ws.xp)
+                kernels.ssm_step(ws.act, ws.xp, R, p["w_dt"].w8, p["w_dt"].scale, ws.xz[:, di:], p["base"],
+                                 st.h[i], ws.xq_i, ws.xs_i)
             ternary_matmul(ws.xq_i, p["w_out"], ws.xs_i, out=ws.out)
             nxt = layers[i + 1] if i + 1 < len(layers) else None
             g, s = (nxt["gamma"], nxt["step"]) if nxt else (pre.gamma_f, pre.step_f)
@@ -108,9 +115,8 @@ class DecodeEngine:
         ternary_matmul(ws.xq_d, pre.w_lm, ws.xs_d, out_scale=pre.out_scale, out=ws.logits)
         kernels.argmax_rows(ws.logits, out=ws.next_ids)
 
-    @staticmethod
-    def launches_per_step(n_layer: int) -> int:
-        return 3 + 6 * n_layer
+    def launches_per_step(self) -> int:
+        return 3 + (4 if self.fused else 6) * self.n_layer
 
     # -- public API -----------------------------------------------------------
     def start(self, prompt_ids: torch.Tensor) -> torch.Tensor:

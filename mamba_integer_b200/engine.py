@@ -5,7 +5,7 @@ sm_100a kernel launches over workspace buffers that are allocated once per
 Per layer (T = batch*seq_len tokens, d = d_model, di = 2*d_model):
     rowprep      residual += out*res_gate; BitShiftNorm; int8 quant   [T, d]
     in_proj      tcgen05 GEMM  [T, d]  x [2di, d]^T  -> xz fp32        [T, 2di]
-    conv_act     conv + ste_clamp + squareplus + int8 quant            [T, di]
+    conv_act     conv + ste_clamp + squareplus + int8 quant (one kernel) [T, di]
     x_proj       tcgen05 GEMM  [T, di] x [R+2N, di]^T -> dt | B | C    [T, R+2N]
     dt quant     int8 quant of the dt columns                          [T, R]
     ssm_scan     dt_proj (int8 dot products by dp4a) / decay / dt / u /
@@ -79,17 +79,17 @@ class _NoTimer:
 
 NO_TIMER = _NoTimer()
 
-# kernel launches of one forward: 1 embedding row pre-pass, 9 per layer, 1 lm_head
+# kernel launches of one forward: 1 embedding row pre-pass, 8 per layer, 1 lm_head
 def launches_per_forward(n_layer: int) -> int:
-    return 2 + 9 * n_layer
+    return 2 + 8 * n_layer
 
 
 def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N: int, timer=NO_TIMER,
               scan_split: int = 0, h_out=None):
     """Everything between the in_proj output (ws.xz) and the out_proj output (ws.out)."""
     with timer("conv_act_quant"):
-        kernels.conv_act_quant(ws.xz, p["conv_w"], p["conv_b"], batch, L, di, act=ws.act, xq=ws.xq_i,
-                               xscale=ws.xs_i, amax_ws=ws.amax)
+        kernels.conv_act_quant_rows(ws.xz, p["conv_w"], p["conv_b"], batch, L, di, act=ws.act, xq=ws.xq_i,
+                                    xscale=ws.xs_i)
     with timer("gemm_x_proj"):
         ternary_matmul(ws.xq_i, p["w_x"], ws.xs_i, out=ws.xp)
     with timer("quant_dt"):

@@ -210,6 +210,26 @@ def conv_act_quant(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, batch:
     return act, xq, xscale
 
 
+def conv_act_quant_rows(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, batch: int, L: int, D: int,
+                        act=None, xq=None, xscale=None):
+    """conv_act_quant in one row-owning kernel (mi_conv_act_quant_rows): same
+    results, no workspace."""
+    T = batch * L
+    if act is None:
+        act = torch.empty(T, D, dtype=torch.float32, device=xz.device)
+    if xq is None:
+        xq = torch.empty(T, D, dtype=torch.int8, device=xz.device)
+    if xscale is None:
+        xscale = torch.empty(T, dtype=torch.float32, device=xz.device)
+    wc = w.detach().to(torch.float32).reshape(D, 4).contiguous()
+    bc = bias.detach().to(torch.float32).contiguous()
+    _lib.check(_lib.load().mi_conv_act_quant_rows(xz.data_ptr(), xz.stride(0), wc.data_ptr(), bc.data_ptr(),
+                                                  act.data_ptr(), xq.data_ptr(), xscale.data_ptr(), batch, L, D,
+                                                  _stream()),
+               "mi_conv_act_quant_rows")
+    return act, xq, xscale
+
+
 def ssm_scan(act, bc, modraw, z, base, batch: int, L: int, y=None, amax=None):
     """Fused selective scan + gate (see mi_ssm_scan).  bc / z may be column
     slices (row stride taken from the tensor)."""
@@ -261,6 +281,19 @@ def ssm_step(act, xp, R: int, w_dt, w_dt_scale, z, base, h, xq, xscale, y=None):
                                        w_dt_scale.data_ptr(), z.data_ptr(), z.stride(0), base.data_ptr(), h.data_ptr(),
                                        _ptr(y), xq.data_ptr(), xscale.data_ptr(), batch, D, N, _stream()),
                "mi_ssm_step")
+
+
+def decode_mid(xz, conv_w, conv_b, win, w_x, w_x_scale, R: int, w_dt, w_dt_scale, base, h, xq, xscale,
+               xp_out=None):
+    """conv step + x_proj + scan step + gate + quantisation for one decode
+    position (see mi_decode_mid); win and h advance in place."""
+    batch = xz.shape[0]
+    D, N = base.shape
+    _lib.check(_lib.load().mi_decode_mid(xz.data_ptr(), xz.stride(0), conv_w.data_ptr(), conv_b.data_ptr(),
+                                         win.data_ptr(), w_x.data_ptr(), w_x_scale.data_ptr(), R, w_dt.data_ptr(),
+                                         w_dt_scale.data_ptr(), base.data_ptr(), h.data_ptr(), _ptr(xp_out),
+                                         xq.data_ptr(), xscale.data_ptr(), batch, D, N, _stream()),
+               "mi_decode_mid")
 
 
 def argmax_rows(x: torch.Tensor, V: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -27,16 +27,17 @@ def _first_argmax(a):
     return np.argmax(a, axis=-1)  # first index of the maximum (no NaN in these logits)
 
 
-@pytest.mark.parametrize("use_graph", [False, True])
+@pytest.mark.parametrize("use_graph,fused", [(False, False), (True, False), (False, True), (True, True)])
 @pytest.mark.parametrize("name,batch,prompt,n_new", [("c1", 3, 20, 5), ("c5s", 2, 2, 4)])
-def test_greedy_decode_equals_full_recompute(cuda_dev, use_graph, name, batch, prompt, n_new):
+def test_greedy_decode_equals_full_recompute(cuda_dev, use_graph, fused, name, batch, prompt, n_new):
     from mamba_integer_b200 import synth
     from mamba_integer_b200.decode import DecodeEngine
     from oracle import model as om
     cfg, sd, _ = cases.model_inputs(name)
     ids = synth.input_ids(cases.MODEL_CASES[name]["base"], batch, prompt)
     m = _model(cfg, sd, cuda_dev)
-    eng = DecodeEngine(m, use_graph=use_graph)
+    eng = DecodeEngine(m, use_graph=use_graph, fused=fused)
+    assert eng.fused == fused
     p = om.prepare(sd)
     seq = ids.numpy()
     logits = eng.start(ids.to(cuda_dev)).cpu().numpy()

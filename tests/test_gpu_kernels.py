@@ -234,6 +234,22 @@ def test_gemm_packed_matches_oracle(cuda_dev, M, N, K):
     _eq(out, out_ref, "scaled fp32 (packed weights)")
 
 
+@pytest.mark.parametrize("M,N,K", [(4736, 1024, 832), (2176, 1152, 832)])  # 256- and 128-wide tiles
+def test_gemm_wide_tiles_both_weight_formats(cuda_dev, M, N, K):
+    """Shapes whose tile count fills the GPU with 256- (N % 256 == 0) or
+    128-wide N tiles; K > 768 keeps them off the A-resident kernel."""
+    k = _mi()
+    g = torch.Generator().manual_seed(M + N)
+    A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
+    W = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8)
+    xs = (torch.rand(M, generator=g) * 0.05 + 1e-3)
+    ws = torch.tensor([2.0 ** -6])
+    out_ref = orc.bitlinear(A.numpy(), xs.numpy(), W.numpy(), 2.0 ** -6)
+    Ad, Wd, xsd, wsd = A.to(cuda_dev), W.to(cuda_dev), xs.to(cuda_dev), ws.to(cuda_dev)
+    _eq(k.bitlinear_i8(Ad, Wd, xsd, wsd), out_ref, "int8 weights")
+    _eq(k.bitlinear_packed(Ad, k.pack_ternary(Wd), xsd, wsd), out_ref, "packed weights")
+
+
 def test_gemm_packed_config3_slice(cuda_dev):
     """Config-3 inputs with the weights packed 2 bits each: a 1024-row slice."""
     from mamba_integer_b200 import synth
@@ -254,7 +270,7 @@ def test_gemm_packed_rejects_k_not_multiple_of_64(cuda_dev):
 
 
 # ---------------------------------------------------------------- conv / ssm / element-wise
-@pytest.mark.parametrize("bsz,L,D", [(2, 37, 512), (1, 130, 1536)])
+@pytest.mark.parametrize("bsz,L,D", [(2, 37, 512), (1, 130, 1536), (3, 67, 100), (1, 5, 4096)])
 def test_conv_act_quant_matches_oracle(cuda_dev, bsz, L, D):
     k = _mi()
     g = torch.Generator().manual_seed(L + D)
@@ -268,6 +284,10 @@ def test_conv_act_quant_matches_oracle(cuda_dev, bsz, L, D):
     _eq(act, act_ref, "act")
     _eq(xq, q_ref, "xq")
     _eq(xs, s_ref, "xscale")
+    act, xq, xs = k.conv_act_quant_rows(xz.to(cuda_dev), w.to(cuda_dev), b.to(cuda_dev), bsz, L, D)
+    _eq(act, act_ref, "act (row kernel)")
+    _eq(xq, q_ref, "xq (row kernel)")
+    _eq(xs, s_ref, "xscale (row kernel)")
 
 
 @pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (3, 5, 160, 16)])
