@@ -203,7 +203,7 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * w_dt int8 [D, ceil16(R)] (zero-padded) and w_dt_scale [1]; each channel
  * forms the exact int32 dot product and the BitLinear rescale
  * acc * (w_dt_scale * dts[t]) itself.  R <= 64.
- * split = lanes per channel (1, 2 or 4; 0 = chosen from batch*D vs the SM
+ * split = lanes per channel (1, 2, 4 or 8; 0 = chosen from batch*D vs the SM
  * count): more lanes per channel keep small per-GPU batches occupied.
  * h_out (optional, [batch, D, N], 16-byte aligned) receives the states after
  * the last position (the starting point of mi_ssm_step).

@@ -496,9 +496,9 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     if (h_out && active) {
         // final states of the sequence [batch, D, 16] (the decode steps continue from them)
-        float4* dst = reinterpret_cast<float4*>(h_out + ((size_t)b * D + d) * NS + sub * NSL);
+        float* dst = h_out + ((size_t)b * D + d) * NS + sub * NSL;
 #pragma unroll
-        for (int i = 0; i < NSL / 4; i++) dst[i] = make_float4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+        for (int i = 0; i < NSL; i++) dst[i] = h[i];
     }
 }
 
@@ -556,7 +556,7 @@ __global__ void __launch_bounds__(SCAN_THREADS)
 ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
                       const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
                       float* __restrict__ amax, float* __restrict__ h_out, int L, int D) {
-    static_assert(S == 2 || S == 4, "split variant");
+    static_assert(S == 2 || S == 4 || S == 8, "split variant");
     constexpr int CHW = 32 / S;   // channels per warp
     constexpr int NSL = NS / S;   // states per lane
     constexpr int SPL = SC / S;   // prologue / gate steps per lane
@@ -572,7 +572,7 @@ ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ b
     const int dd = active ? d : 0;
     const size_t row0 = (size_t)b * L;
     // lanes with the same sub-index: (lane % S == s) <=> bit pattern
-    constexpr unsigned SUBMASK0 = S == 2 ? 0x55555555u : 0x11111111u;
+    constexpr unsigned SUBMASK0 = S == 2 ? 0x55555555u : S == 4 ? 0x11111111u : 0x01010101u;
 
     int32_t wd[RW > 0 ? RW : 1];
     float wsc = 0.0f;
@@ -672,9 +672,13 @@ ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ b
                     h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
                 }
             }
+            if (NSL % 4 == 0) {
 #pragma unroll
-            for (int i = 0; i < NSL; i += 4)
-                *reinterpret_cast<float4*>(&snap[j][lane][i]) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+                for (int i = 0; i < NSL; i += 4)
+                    *reinterpret_cast<float4*>(&snap[j][lane][i]) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+            } else {
+                *reinterpret_cast<float2*>(&snap[j][lane][0]) = make_float2(h[0], h[1]);
+            }
         }
         __syncwarp();
         // (B2) y = matmul(h, C[..., None]): fused multiply-add over n = 0..15 from 0   (:440)
@@ -728,9 +732,9 @@ ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ b
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     if (h_out && active) {
         // final states of the sequence [batch, D, 16] (the decode steps continue from them)
-        float4* dst = reinterpret_cast<float4*>(h_out + ((size_t)b * D + d) * NS + sub * NSL);
+        float* dst = h_out + ((size_t)b * D + d) * NS + sub * NSL;
 #pragma unroll
-        for (int i = 0; i < NSL / 4; i++) dst[i] = make_float4(h[4 * i], h[4 * i + 1], h[4 * i + 2], h[4 * i + 3]);
+        for (int i = 0; i < NSL; i++) dst[i] = h[i];
     }
 }
 
@@ -805,8 +809,11 @@ static void launch_scan(int split, int batch, int L, int D, const float* act, co
     else if (split == 2)
         ssm_scan_split_kernel<RW, 2><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out,
                                                                    L, D);
-    else
+    else if (split == 4)
         ssm_scan_split_kernel<RW, 4><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out,
+                                                                   L, D);
+    else
+        ssm_scan_split_kernel<RW, 8><<<grid, SCAN_THREADS, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out,
                                                                    L, D);
 }
 
@@ -836,7 +843,7 @@ extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const
     if (!act || !bc || !dtq || !dts || !w_dt || !w_dt_scale || !z || !base || !y) return MI_ERR_INVALID;
     if (N != mi::ssm::NS) return MI_ERR_UNSUPPORTED;
     if (batch <= 0 || L <= 0 || D <= 0 || R <= 0 || ldbc < 2 * N || ldz < D) return MI_ERR_INVALID;
-    if (split != 0 && split != 1 && split != 2 && split != 4) return MI_ERR_INVALID;
+    if (split != 0 && split != 1 && split != 2 && split != 4 && split != 8) return MI_ERR_INVALID;
     const int R16 = (R + 15) / 16 * 16;
     if (R16 > 4 * mi::ssm::MAX_RW || ldq < R16 || (ldq & 15)) return MI_ERR_UNSUPPORTED;
     if (batch > 65535) return MI_ERR_UNSUPPORTED;

@@ -313,7 +313,7 @@ def test_ssm_scan_matches_oracle(cuda_dev, bsz, L, D, R):
     _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
 
 
-@pytest.mark.parametrize("split", [1, 2, 4, 0])
+@pytest.mark.parametrize("split", [1, 2, 4, 8, 0])
 @pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (2, 9, 96, 64), (1, 33, 72, 20)])
 def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split):
     """dt_proj fused into the scan: same result as quantise -> BitLinear -> scan."""
