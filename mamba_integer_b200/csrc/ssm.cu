@@ -355,6 +355,10 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
     }
 #pragma unroll
     for (int i = 0; i < NSL; i++) h[i] = 0.0f;
+    // ste_clamp(., -20, 20) returns values within 20 + 16 of 0 (its error is half an
+    // ulp of the input, and inputs whose ulp exceeds 32 give exactly 0), so for bases
+    // in [37, 63963] the range conditions of the fast path below always hold
+    const bool wide_ok = !bnan && (bmin >= 37.0f) && (bmax <= 63963.0f);
 
     const int nchunks = cdiv(L, SC);
     scan_stage_load<RW, CHW>(stage[0], act, src, z, bc, ldbc, ldz, row0, 0, L, d0, D);
@@ -407,8 +411,10 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
             // so the channel's extreme bases decide.  base >= 1 and a mod that is 0 or
             // not tiny keep base/2^15 and mod/2^15 exact (no subnormals), and with
             // base + mod >= 0 for every state the lower bound cannot bind.
-            const bool inside = !bnan && (bmin >= 1.0f) && (__fadd_rn(bmin, mod) >= 0.0f) &&
-                                (__fadd_rn(bmax, mod) <= 64000.0f) && (mod == 0.0f || fabsf(mod) >= 1e-30f);
+            bool inside = (mod == 0.0f || fabsf(mod) >= 1e-30f);  // false for NaN
+            if (!wide_ok)
+                inside = inside && !bnan && (bmin >= 1.0f) && (__fadd_rn(bmin, mod) >= 0.0f) &&
+                         (__fadd_rn(bmax, mod) <= 64000.0f);
             if (__all_sync(0xffffffffu, inside)) fast_mask |= 1u << j;
             if (S == 1) {  // each lane owns its column: write back at once (fewer live registers)
                 st.mod[j][ch] = modr[j];
@@ -480,16 +486,34 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
             m[j] = (j < tn && owner) ? __float_as_uint(fabsf(out)) : 0u;
         }
         if (amax) {
+            // fp32 bits of non-negative values order like unsigned ints (NaN above +inf).
+            // Reduce-scatter over the warp: at offsets 16, 8, 4 each lane keeps half
+            // of its steps and takes the other half's partner values (9 shuffles for
+            // the 8 steps instead of 40); lane 4s + ... ends with step
+            // 4*bit4 + 2*bit3 + bit2 of its index.
+            static_assert(SC == 8, "reduce-scatter below is written for 8 steps");
+            const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+            unsigned m2[4], m3[2];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-                for (int j = 0; j < SC; j++) m[j] = max(m[j], __shfl_xor_sync(0xffffffffu, m[j], o));
+            for (int i = 0; i < 4; i++) {
+                const unsigned send = b4 ? m[i] : m[4 + i], keep = b4 ? m[4 + i] : m[i];
+                m2[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, 16));
             }
-            // fp32 bits of non-negative values order like unsigned ints (NaN above +inf)
-            unsigned mine = 0u;  // lane j publishes step j
 #pragma unroll
-            for (int j = 0; j < SC; j++) mine = (lane == j) ? m[j] : mine;
-            if (lane < tn) atomicMax(reinterpret_cast<unsigned int*>(amax) + row0 + t0 + lane, mine);
+            for (int i = 0; i < 2; i++) {
+                const unsigned send = b3 ? m2[i] : m2[2 + i], keep = b3 ? m2[2 + i] : m2[i];
+                m3[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+            }
+            unsigned m4;
+            {
+                const unsigned send = b2 ? m3[0] : m3[1], keep = b2 ? m3[1] : m3[0];
+                m4 = max(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+            }
+            m4 = max(m4, __shfl_xor_sync(0xffffffffu, m4, 2));
+            m4 = max(m4, __shfl_xor_sync(0xffffffffu, m4, 1));
+            const int jstep = (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0);
+            if ((lane & 3) == 0 && jstep < tn)
+                atomicMax(reinterpret_cast<unsigned int*>(amax) + row0 + t0 + jstep, m4);
         }
         __syncwarp();  // the buffer is refilled by the next iteration's copies
     }
