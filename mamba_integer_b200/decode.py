@@ -130,6 +130,28 @@ class DecodeEngine:
             self._graph = None
         return pre.forward(prompt_ids.to(pre.dev), states=self.states, last_only=True)
 
+    def reserve(self, batch: int) -> None:
+        """Allocate (zeroed) state and step buffers for `batch` stream slots
+        without running a prompt; prompts then enter slots with prefill_slots."""
+        pre = self.pre
+        if self.states is None or self.states.batch != batch:
+            self.states = StreamStates(self.n_layer, batch, pre.di, pre.N, pre.dev)
+            self.ws = _StepWorkspace(batch, pre.d, pre.di, pre.R, pre.N, pre.V, pre.dev)
+            self._graph = None
+
+    def prefill_slots(self, slots, prompt_ids: torch.Tensor) -> torch.Tensor:
+        """Run k prompts of one length [k, L] through the prefill kernels and put
+        their streams' state into the given slots (the other slots are left as
+        they are); returns their last-position logits [k, V]."""
+        pre = self.pre
+        k = prompt_ids.shape[0]
+        tmp = StreamStates(self.n_layer, k, pre.di, pre.N, pre.dev)
+        logits = pre.forward(prompt_ids.to(pre.dev), states=tmp, last_only=True)
+        idx = torch.as_tensor(list(slots), dtype=torch.int64, device=pre.dev)
+        self.states.win.index_copy_(1, idx, tmp.win)
+        self.states.h.index_copy_(1, idx, tmp.h)
+        return logits
+
     def step(self, ids: torch.Tensor) -> torch.Tensor:
         """Feed one token per stream (int64 [batch]); returns the logits of the
         new position [batch, V] (a buffer reused by the next step)."""
@@ -156,6 +178,11 @@ class DecodeEngine:
             self._launch_step()
         torch.cuda.current_stream().wait_stream(stream)
         self._graph = g
+
+    @staticmethod
+    def argmax(logits: torch.Tensor) -> torch.Tensor:
+        """Greedy choice over logits [k, V] (int64 [k])."""
+        return kernels.argmax_rows(logits)
 
     def next_ids(self) -> torch.Tensor:
         """argmax of the logits of the last step (int64 [batch])."""
