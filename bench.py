@@ -280,6 +280,43 @@ def decode_metrics(dev, steps: int = 64, warmup: int = 3, batch: int | None = No
             "launches_per_step": eng.launches_per_step(), "cuda_graph": True}
 
 
+def server_metrics(dev, n_requests: int = 384, slots: int = 256, max_new: int = 32, seed: int = 5):
+    """Config-5 model behind the continuous-batching server: n_requests Zipf
+    prompts of lengths drawn from {32, 64, 128, 256}, max_new tokens each,
+    `slots` streams resident.  Wall time of the whole run (prefills,
+    graph-replayed steps, the per-step host loop) between two device syncs."""
+    import time
+    from mamba_integer_b200 import synth
+    from mamba_integer_b200.mamba_integer_model import MambaIntegerModel
+    from mamba_integer_b200.serve import DecodeServer
+
+    c = synth.CONFIGS["c5"]
+    cfg = synth.model_config("c5")
+    model = MambaIntegerModel(cfg)
+    model.load_state_dict(synth.model_state_dict(cfg, c["seed"]))
+    model = model.to(dev).eval()
+    g = torch.Generator().manual_seed(seed)
+    lens = [32, 64, 128, 256]
+    prompts = [synth.zipf_ids(1, lens[int(torch.randint(0, 4, (1,), generator=g))], cfg["vocab_size"], g)[0].tolist()
+               for _ in range(n_requests)]
+    warm = DecodeServer(model, slots=slots)  # capture the step graph and warm the prefill shapes
+    for n in lens:
+        warm.submit(prompts[0][:1] * n, 2)
+    warm.run()
+    srv = DecodeServer(model, slots=slots, engine=warm.eng)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for pr in prompts:
+        srv.submit(pr, max_new)
+    out = srv.run()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    gen = sum(len(v) for v in out.values())
+    return {"config": f"config5 model, {n_requests} requests (prompts 32-256 tokens, {max_new} new each), "
+                      f"{slots} slots, greedy", "generated_tokens": gen, "wall_s": wall, "tok_per_s": gen / wall,
+            "decode_steps": srv.steps, "prompt_tokens": sum(len(p) for p in prompts)}
+
+
 def cpu_baseline(n_tokens: int = 256, threads: int = 0):
     """The CPU restatement of the reference path (full 24 layers + lm_head) on
     one sequence of n_tokens of the config-4 workload."""
@@ -447,6 +484,7 @@ def main():
             torch.cuda.empty_cache()
             secondary = secondary_metrics(dev)
             secondary["decode"] = decode_metrics(dev)
+            secondary["server"] = server_metrics(dev)
 
     hbm, bf16, src = peaks()
     totals = {k: sum(v) for k, v in per_k.items()}
