@@ -87,6 +87,7 @@ class BitLinear(nn.Module):
         else:
             self.register_parameter("bias", None)
         self._cache = None  # (TernaryWeights, weight version, device)
+        self._fixed = None  # (int8 {-1,0,1} [out, in], scale): quantised weights given directly
 
     # -- weight cache -------------------------------------------------------
     def device_weights(self, device=None) -> TernaryWeights:
@@ -96,7 +97,10 @@ class BitLinear(nn.Module):
         ver = self.weight._version
         c = self._cache
         if c is None or c[1] != ver or c[2] != device:
-            wq, scale = weight_quant_ternary(self.weight)
+            if self._fixed is not None:
+                wq, scale = self._fixed[0].to(torch.float32), self._fixed[1]
+            else:
+                wq, scale = weight_quant_ternary(self.weight)
             K16 = _pad16(self.in_features)
             w8 = torch.zeros(self.out_features, K16, dtype=torch.int8)
             w8[:, : self.in_features] = wq.to(torch.int8)
@@ -107,8 +111,23 @@ class BitLinear(nn.Module):
 
     @torch.no_grad()
     def get_ternary_weights(self) -> Tuple[torch.Tensor, torch.Tensor]:
+        if self._fixed is not None:
+            return self._fixed[0].clone(), self._fixed[1].clone()
         wq, scale = weight_quant_ternary(self.weight)
         return wq.to(torch.int8), scale
+
+    @torch.no_grad()
+    def set_ternary(self, wq: torch.Tensor, scale) -> None:
+        """Use already-quantised weights (int8 {-1,0,1} [out, in] and the
+        absmean scale), e.g. from the reference's int8 export, instead of
+        quantising ``weight``; ``weight`` is set to wq * scale."""
+        wq = torch.as_tensor(wq).to(torch.int8).reshape(self.out_features, self.in_features).cpu()
+        if bool(((wq < -1) | (wq > 1)).any()):
+            raise ValueError("ternary weights must be in {-1, 0, 1}")
+        scale = torch.as_tensor(scale, dtype=torch.float32).reshape(()).cpu()
+        self._fixed = (wq, scale)
+        self.weight.copy_((wq.to(torch.float32) * scale).to(self.weight.device))
+        self._cache = None
 
     # -- forward ------------------------------------------------------------
     def forward(self, x: torch.Tensor) -> torch.Tensor:
