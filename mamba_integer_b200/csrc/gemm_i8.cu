@@ -878,7 +878,14 @@ static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_sca
     if (((uintptr_t)out) & 15) return MI_ERR_INVALID;
     if (K > 132104) return MI_ERR_UNSUPPORTED;
     cudaStream_t s = (cudaStream_t)stream;
-    if (K <= ARES_MAXK * BK && N > 128)  // wide outputs over a short K: keep A resident
+    const int sms = sm_count();
+    const long long tm = cdiv(M, BM);
+    auto fills = [&](int bn) { return tm * cdiv(N, bn) >= sms; };
+    // 256-wide tiles run the tensor cores at about twice the rate of 128-wide
+    // ones; when N allows them they win even though A is then re-read from L2
+    // for every N tile.  Otherwise wide outputs over a short K keep A resident.
+    const bool wide256 = N % 256 == 0 && fills(256);
+    if (!wide256 && K <= ARES_MAXK * BK && N > 128)
         return launch_ares<PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (N <= 128 && N % 16 == 0 && N != 128) {
         // narrow projections (x_proj: N = dt_rank + 2*d_state) in one N tile
@@ -890,10 +897,7 @@ static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_sca
     }
     // the widest N tile that still gives every SM a tile (few-row GEMMs, e.g.
     // decoding, get narrower tiles and more CTAs)
-    const int sms = sm_count();
-    const long long tm = cdiv(M, BM);
-    auto fills = [&](int bn) { return tm * cdiv(N, bn) >= sms; };
-    if (N % 256 == 0 && fills(256))
+    if (wide256)
         return launch<256, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (fills(128))
         return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);

@@ -3,6 +3,7 @@
     python -m mamba_integer_b200.workloads config2            # integer scan, config 2
     python -m mamba_integer_b200.workloads config3            # BitLinear, int8 weights
     python -m mamba_integer_b200.workloads config3-packed     # BitLinear, 2-bit packed weights
+    python -m mamba_integer_b200.workloads config4-in_proj    # one in_proj of the config-4 prefill
     python -m mamba_integer_b200.workloads config5-step       # one decode step, config 5 shapes
 
 Each runs its kernel(s) ``--launches`` times (default 2: a warm-up launch, then
@@ -44,6 +45,22 @@ def _config3(dev, launches: int, packed: bool) -> None:
             kernels.bitlinear_i8(A, Wq, out=C)
 
 
+def _config4_in_proj(dev, launches: int) -> None:
+    """One layer's in_proj of the config-4 prefill at full size: int8 A
+    [131072, 768] x packed ternary W [3072, 768] -> fp32 [131072, 3072] with
+    the BitLinear rescale (the model's A-resident GEMM)."""
+    g = torch.Generator().manual_seed(3)
+    M, N, K = 64 * 2048, 3072, 768
+    A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(dev)
+    W = synth.ternary_weight(N, K, g)
+    Wp = kernels.pack_ternary((W * 32).to(torch.int8).to(dev))
+    xs = (torch.rand(M, generator=g) * 0.05 + 1e-3).to(dev)
+    ws = torch.tensor([2.0 ** -6], device=dev)
+    out = torch.empty(M, N, device=dev)
+    for _ in range(launches):
+        kernels.bitlinear_packed(A, Wp, xs, ws, out=out)
+
+
 def _config5_step(dev, launches: int) -> None:
     """Decode steps of 256 streams after a short prompt (the per-step work does
     not depend on the prompt length), launched eagerly, without a CUDA graph."""
@@ -65,6 +82,7 @@ CASES = {
     "config2": lambda dev, k: _config2(dev, k),
     "config3": lambda dev, k: _config3(dev, k, packed=False),
     "config3-packed": lambda dev, k: _config3(dev, k, packed=True),
+    "config4-in_proj": lambda dev, k: _config4_in_proj(dev, k),
     "config5-step": lambda dev, k: _config5_step(dev, k),
 }
 

@@ -234,10 +234,11 @@ def test_gemm_packed_matches_oracle(cuda_dev, M, N, K):
     _eq(out, out_ref, "scaled fp32 (packed weights)")
 
 
-@pytest.mark.parametrize("M,N,K", [(4736, 1024, 832), (2176, 1152, 832)])  # 256- and 128-wide tiles
+@pytest.mark.parametrize("M,N,K", [(4736, 1024, 832), (2176, 1152, 832), (4736, 1024, 768), (300, 1152, 768)])
 def test_gemm_wide_tiles_both_weight_formats(cuda_dev, M, N, K):
-    """Shapes whose tile count fills the GPU with 256- (N % 256 == 0) or
-    128-wide N tiles; K > 768 keeps them off the A-resident kernel."""
+    """Kernel choices by shape: 256-wide tiles (N % 256 == 0 and enough
+    tiles), 128-wide tiles, and the A-resident kernel (K <= 768, N > 128, no
+    256-wide tiling)."""
     k = _mi()
     g = torch.Generator().manual_seed(M + N)
     A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8)
