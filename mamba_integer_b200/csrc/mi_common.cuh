@@ -122,6 +122,46 @@ __device__ __forceinline__ float squareplus_bounded(float x) {
     return __fmul_rn(0.5f, __fadd_rn(x, s));
 }
 
+// Two independent elements at once with f32x2 operations (each component
+// rounds exactly as the scalar operation).  An f32x2 add or FMA whose operand
+// is an f32x2 product is contracted by the compiler (dropping the product's
+// rounding), so every addition that follows a product stays scalar; additions
+// of clamp results (min/max outputs) are safe.
+//
+// ste_clamp of a pair that is NOT an f32x2 product (its two adds would be
+// fused with the product); clamp results and FMA sums are fine.
+__device__ __forceinline__ float2 ste_clamp2(float2 x, float lo, float hi) {
+    const float2 c = make_float2(clamp_t(x.x, lo, hi), clamp_t(x.y, lo, hi));
+    const float2 d = __fadd2_rn(c, make_float2(-x.x, -x.y));  // clamp(x) - x
+    return __fadd2_rn(x, d);
+}
+
+// squareplus_bounded of a pair
+__device__ __forceinline__ float2 squareplus_bounded2(float2 x) {
+    const float2 xx = __fmul2_rn(x, x);
+    const float2 y = make_float2(__fadd_rn(xx.x, 4.0f), __fadd_rn(xx.y, 4.0f));
+    float2 r;
+    r.x = (y.x > 16.0f) ? 0.125f : 0.5f;
+    r.x = (y.x > 64.0f) ? 0.0625f : r.x;
+    r.x = (y.x > 256.0f) ? 0.03125f : r.x;
+    r.y = (y.y > 16.0f) ? 0.125f : 0.5f;
+    r.y = (y.y > 64.0f) ? 0.0625f : r.y;
+    r.y = (y.y > 256.0f) ? 0.03125f : r.y;
+    const float2 half = make_float2(0.5f, 0.5f);
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        float2 t = __fmul2_rn(half, y);
+        t = __fmul2_rn(t, r);
+        t = __fmul2_rn(t, r);
+        t = make_float2(__fsub_rn(1.5f, t.x), __fsub_rn(1.5f, t.y));
+        r = __fmul2_rn(r, t);
+        r = make_float2(clamp_t(r.x, 1e-6f, 1e3f), clamp_t(r.y, 1e-6f, 1e3f));
+    }
+    const float2 p = __fmul2_rn(y, r);
+    const float2 sq = make_float2(clamp_t(p.x, 0.0f, 1e3f), clamp_t(p.y, 0.0f, 1e3f));
+    return __fmul2_rn(half, __fadd2_rn(x, sq));
+}
+
 // y * _sigmoid_algebraic(z) = y * (0.5 + (0.5*z) / (1 + |z|))  (:124-132, :444)
 __device__ __forceinline__ float sigmoid_gate(float y, float z) {
     float num = __fmul_rn(0.5f, z);

@@ -105,9 +105,14 @@ conv_act_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__
 // conv_act_kernel followed by quant_rows_kernel.
 constexpr int CONVR_G = 4;  // positions per group (one block reduction each group)
 
-__global__ void __launch_bounds__(1024)
+// MAXT = the CTA size it is compiled for: up to 384 threads (D <= 1536) it
+// gets up to 80 registers at two CTAs per SM and computes the channels in
+// f32x2 pairs; up to 1024 threads it stays within 64 registers, scalar.
+template <int MAXT>
+__global__ void __launch_bounds__(MAXT, MAXT <= 384 ? 2 : 1)
 conv_rows_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w, const float* __restrict__ bias,
                  float* __restrict__ act, int8_t* __restrict__ xq, float* __restrict__ xscale, int L, int D) {
+    constexpr bool PAIRED = MAXT <= 384;
     __shared__ unsigned red[2][CONVR_G][32];  // per position: each warp's max |act| bits (double buffer)
     const int c = 4 * threadIdx.x;  // first of this thread's 4 channels
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -136,10 +141,27 @@ conv_rows_kernel(const float* __restrict__ xz, int ldx, const float* __restrict_
 #pragma unroll
         for (int j = 0; j < CONVR_G; j++) {
             const float4 xv = a[j];
-            a[j].x = conv_tap4(bs.x, wv[0], w0.x, w1.x, w2.x, xv.x);
-            a[j].y = conv_tap4(bs.y, wv[1], w0.y, w1.y, w2.y, xv.y);
-            a[j].z = conv_tap4(bs.z, wv[2], w0.z, w1.z, w2.z, xv.z);
-            a[j].w = conv_tap4(bs.w, wv[3], w0.w, w1.w, w2.w, xv.w);
+            if (PAIRED) {
+                // channels (x, y) and (z, w) in pairs: the FMA taps (bias first,
+                // k = 0..3), ste_clamp and squareplus as f32x2
+                float2 p = make_float2(bs.x, bs.y), q = make_float2(bs.z, bs.w);
+                p = __ffma2_rn(make_float2(wv[0].x, wv[1].x), make_float2(w0.x, w0.y), p);
+                q = __ffma2_rn(make_float2(wv[2].x, wv[3].x), make_float2(w0.z, w0.w), q);
+                p = __ffma2_rn(make_float2(wv[0].y, wv[1].y), make_float2(w1.x, w1.y), p);
+                q = __ffma2_rn(make_float2(wv[2].y, wv[3].y), make_float2(w1.z, w1.w), q);
+                p = __ffma2_rn(make_float2(wv[0].z, wv[1].z), make_float2(w2.x, w2.y), p);
+                q = __ffma2_rn(make_float2(wv[2].z, wv[3].z), make_float2(w2.z, w2.w), q);
+                p = __ffma2_rn(make_float2(wv[0].w, wv[1].w), make_float2(xv.x, xv.y), p);
+                q = __ffma2_rn(make_float2(wv[2].w, wv[3].w), make_float2(xv.z, xv.w), q);
+                p = squareplus_bounded2(ste_clamp2(p, -50.0f, 50.0f));
+                q = squareplus_bounded2(ste_clamp2(q, -50.0f, 50.0f));
+                a[j] = make_float4(p.x, p.y, q.x, q.y);
+            } else {
+                a[j].x = conv_tap4(bs.x, wv[0], w0.x, w1.x, w2.x, xv.x);
+                a[j].y = conv_tap4(bs.y, wv[1], w0.y, w1.y, w2.y, xv.y);
+                a[j].z = conv_tap4(bs.z, wv[2], w0.z, w1.z, w2.z, xv.z);
+                a[j].w = conv_tap4(bs.w, wv[3], w0.w, w1.w, w2.w, xv.w);
+            }
             w0 = w1;
             w1 = w2;
             w2 = xv;
@@ -798,7 +820,12 @@ extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, 
     if (batch > 65535) return MI_ERR_UNSUPPORTED;
     const int threads = mi::cdiv(D / 4, 32) * 32;
     dim3 grid(mi::cdiv(L, mi::ssm::CONV_TC), batch);
-    mi::ssm::conv_rows_kernel<<<grid, threads, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale, L, D);
+    if (threads <= 384)
+        mi::ssm::conv_rows_kernel<384><<<grid, threads, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale, L,
+                                                                                  D);
+    else
+        mi::ssm::conv_rows_kernel<1024><<<grid, threads, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale,
+                                                                                   L, D);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
