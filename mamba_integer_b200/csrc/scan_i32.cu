@@ -6,7 +6,8 @@
 // The state update follows the reference POC kernel
 // (src/cuda_kernels/dyadic_mamba_kernel.cu:53-59: 64-bit product, arithmetic
 // right shift, add) with the selective-scan input term B_t*x_t and the output
-// contraction C_t.h_t added.
+// contraction C_t.h_t added.  The shifted product is formed as the high word
+// of a 32-bit multiply (see scan_step), which gives the same integer.
 //
 // Layout / parallelism: one warp per CTA owns 32/LPC channels of one
 // sequence; LPC lanes per channel each hold 16/LPC of the 16 int32 states in
@@ -14,19 +15,24 @@
 // independent (sequence, channel, state) chains are all the parallelism there
 // is).  x and B|C arrive through a per-warp 4-deep cp.async ring of TC-step
 // chunks (three chunks in flight ahead of the one in use, no block-level
-// barriers).  Each lane folds its states' C*h into y with 64-bit
-// multiply-adds, the LPC partial sums meet in shuffles, y is staged in shared
-// memory and written as 16-byte vectors.  n stays in registers.  LPC = 2 at
-// config 2 sizes: the B|C values every lane must receive each step (a 16-byte
-// shared load delivers 512 bytes per warp) and the y shuffles share one
-// load/store data path, which fewer lanes per channel use less of per state
-// update.
+// barriers).  A full chunk runs as one unrolled block, so that the loads and
+// y sums of a step overlap the state chains of the next ones (the kernel is
+// bound by dependency latency: few warps per SM, each a serial recurrence).
+// Each lane's partial y sum is staged in shared memory; the writer adds the
+// LPC partials of a channel and stores 16-byte vectors.  LPC = 2 at config 2
+// sizes: the B|C values every lane must receive each step share the
+// load/store data path, which fewer lanes per channel use less of.
 //
-// Exactness: the shifted product fits int32 whenever 0 <= n <= 2^k (so the
-// 64-bit shift result is truncated losslessly); |B*x| < 2^30 when
-// |B|,|x| <= 32767; the state add is checked for int32 overflow with a sign
-// test and y is accumulated in 64 bits.  Violations set the device error word
-// instead of producing wrong values silently.
+// Exactness: the shifted product fits int32 whenever 0 <= n <= 2^k, and its
+// magnitude never exceeds |h|; |B*x| < 2^30 when |B|,|x| <= 32767.  Per chunk,
+// the staged inputs' largest magnitudes and the warp's largest state bound
+// every state and every y partial sum of the chunk; where that bound fits
+// int32 the chunk runs with 32-bit arithmetic only, otherwise each state add
+// is checked for int32 overflow with a sign test and y is summed in 64 bits.
+// Violations set the device error word instead of producing wrong values
+// silently.
+#include <type_traits>
+
 #include "mi_common.cuh"
 
 namespace mi {
@@ -42,6 +48,7 @@ struct Geo {
     static constexpr int SPL = NS / LPC;  // states per lane
     static constexpr int CH = 32 / LPC;   // channels per warp
     static constexpr int XQ = CH / 4;     // 16-byte chunks per staged x row
+    static constexpr int P = LPC < 2 ? LPC : 2;  // partial y sums staged per channel
 };
 
 template <int CH>
@@ -82,21 +89,98 @@ __device__ __forceinline__ void load_chunk(Stage<CH>& st, int t0, const int32_t*
     }
 }
 
+// One time step of one lane's SPL states; its partial y sum goes to ys_row
+// (P partials per channel, summed by the writer: no shuffle on the step's
+// path except one for 4 lanes per channel).
+//
+// The shifted product floor(h * n / 2^k) is the high word of h * (n * 2^(32-k)):
+// with m = n << (32 - k) taken as a signed int32, mul.hi gives
+// floor(h * m / 2^32), which is 2^32 * h too small exactly when n * 2^(32-k)
+// >= 2^31 (m wrapped negative, or to 0 for n = 2^k), so the lane adds h there
+// (am = -1 selects it).  0 <= n <= 2^k keeps |result| <= |h|.
+//
+// FAST: the chunk's bound (checked by the caller) rules out every int32
+// overflow of the states and of 32-bit y sums, so neither is tested or
+// widened.  Otherwise the y sums are 64-bit and each state add is checked.
+template <int LPC, bool FAST>
+__device__ __forceinline__ void scan_step(int32_t (&h)[Geo<LPC>::SPL], const int32_t (&nm)[Geo<LPC>::SPL],
+                                          const int32_t (&am)[Geo<LPC>::SPL], int32_t xv,
+                                          const int32_t* __restrict__ bc_row, int ch, int sub,
+                                          int64_t* __restrict__ ys_row, int32_t& ovf) {
+    constexpr int SPL = Geo<LPC>::SPL, P = Geo<LPC>::P;
+    constexpr int NACC = SPL < 4 ? SPL : 4;  // independent multiply-add chains for y
+    int32_t bb[SPL], cc[SPL];
+#pragma unroll
+    for (int q = 0; q < SPL / 4; q++) {
+        const int4 b4 = *reinterpret_cast<const int4*>(&bc_row[sub * SPL + 4 * q]);
+        const int4 c4 = *reinterpret_cast<const int4*>(&bc_row[NS + sub * SPL + 4 * q]);
+        bb[4 * q] = b4.x; bb[4 * q + 1] = b4.y; bb[4 * q + 2] = b4.z; bb[4 * q + 3] = b4.w;
+        cc[4 * q] = c4.x; cc[4 * q + 1] = c4.y; cc[4 * q + 2] = c4.z; cc[4 * q + 3] = c4.w;
+    }
+    // integer sums are exact in any order
+    using Acc = typename std::conditional<FAST, int32_t, long long>::type;
+    Acc acc[NACC];
+#pragma unroll
+    for (int a = 0; a < NACC; a++) acc[a] = 0;
+    int32_t ovl = 0;
+#pragma unroll
+    for (int j = 0; j < SPL; j++) {
+        const int32_t s = __mulhi(h[j], nm[j]) + (h[j] & am[j]);
+        const int32_t bx = (int32_t)((uint32_t)bb[j] * (uint32_t)xv);  // |B*x| < 2^30 when in range
+        const int32_t hn = (int32_t)((uint32_t)s + (uint32_t)bx);
+        if (!FAST) ovl |= (s ^ hn) & (bx ^ hn);
+        h[j] = hn;
+        acc[j % NACC] += (Acc)cc[j] * (Acc)hn;
+    }
+    if (!FAST) ovf |= ovl;
+#pragma unroll
+    for (int w = NACC / 2; w >= 1; w /= 2)
+#pragma unroll
+        for (int a = 0; a < w; a++) acc[a] += acc[a + w];
+    long long y = acc[0];
+    if (LPC == 4) y += __shfl_xor_sync(0xffffffffu, y, 1);
+    if (LPC != 4 || (sub & 1) == 0) ys_row[ch * P + (LPC == 4 ? sub >> 1 : sub)] = y;
+}
+
 __device__ __forceinline__ int out_of_range4(int4 v) {
     // |v| > 32767 for any component (the preconditions of the exact int32 path)
     return ((unsigned)v.x + 32767u > 65534u) | ((unsigned)v.y + 32767u > 65534u) |
            ((unsigned)v.z + 32767u > 65534u) | ((unsigned)v.w + 32767u > 65534u);
 }
 
+__device__ __forceinline__ unsigned uabs(int32_t v) {
+    const unsigned u = (unsigned)v;
+    return v < 0 ? 0u - u : u;  // 2^31 for INT32_MIN
+}
+__device__ __forceinline__ unsigned absmax4(int4 v) {
+    return max(max(uabs(v.x), uabs(v.y)), max(uabs(v.z), uabs(v.w)));
+}
+
+// The steps of one staged chunk (tn of them).
+template <int LPC, bool FAST, int CH, int P>
+__device__ __forceinline__ void scan_chunk(int32_t (&h)[Geo<LPC>::SPL], const int32_t (&nm)[Geo<LPC>::SPL],
+                                           const int32_t (&am)[Geo<LPC>::SPL], const Stage<CH>& st,
+                                           int64_t (&ys)[TC][CH * P], int tn, int ch, int sub, int32_t& ovf) {
+    if (tn == TC) {
+        // a full chunk as one straight-line block: the steps' loads and y sums
+        // overlap the state chains of the following steps
+#pragma unroll
+        for (int r = 0; r < TC; r++) scan_step<LPC, FAST>(h, nm, am, st.x[r][ch], st.bc[r], ch, sub, ys[r], ovf);
+    } else {
+#pragma unroll 1
+        for (int r = 0; r < tn; r++) scan_step<LPC, FAST>(h, nm, am, st.x[r][ch], st.bc[r], ch, sub, ys[r], ovf);
+    }
+}
+
 template <int LPC, bool Y64>
 __global__ void __launch_bounds__(THREADS)
 scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, const int32_t* __restrict__ Cm,
-                const int32_t* __restrict__ n, int k, int32_t* __restrict__ y32, int64_t* __restrict__ y64,
+                const int32_t* __restrict__ n, const int k, int32_t* __restrict__ y32, int64_t* __restrict__ y64,
                 int32_t* __restrict__ h_io, int L, int D) {
     using G = Geo<LPC>;
-    constexpr int SPL = G::SPL, CH = G::CH;
+    constexpr int SPL = G::SPL, CH = G::CH, P = G::P;
     __shared__ __align__(16) Stage<CH> stage[SST];
-    __shared__ __align__(16) int64_t ys[TC][CH];
+    __shared__ __align__(16) int64_t ys[TC][CH * P];  // partial y sums of the chunk
     const int lane = threadIdx.x;
     const int b = blockIdx.y;
     const int d0 = blockIdx.x * CH;
@@ -106,15 +190,18 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
     const bool active = d < D;
     const size_t row0 = (size_t)b * L;
 
-    int32_t h[SPL], nn[SPL];
+    // states, and each n as the multiplier n << (32 - k) and the add-back mask
+    int32_t h[SPL], nm[SPL], am[SPL];
     int bad = 0;
     const int32_t lim = 1 << k;
 #pragma unroll
     for (int j = 0; j < SPL; j++) {
         const int jj = sub * SPL + j;
         h[j] = active ? h_io[((size_t)b * D + d) * NS + jj] : 0;
-        nn[j] = active ? n[(size_t)d * NS + jj] : 0;
-        bad |= (nn[j] < 0) | (nn[j] > lim);
+        const int32_t nv = active ? n[(size_t)d * NS + jj] : 0;
+        bad |= (nv < 0) | (nv > lim);
+        nm[j] = (int32_t)((uint32_t)nv << (32 - k));
+        am[j] = (nv >= (lim >> 1)) ? -1 : 0;
     }
 
     int ovf = 0;  // sign-test accumulator: negative => an int32 state or y32 overflowed
@@ -132,46 +219,41 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
         asm volatile("cp.async.commit_group;\n" ::: "memory");
         asm volatile("cp.async.wait_group %0;\n" ::"n"(SST - 1) : "memory");
         __syncwarp();
-        // range check of the staged inputs
+        // range check of the staged inputs, and their largest magnitudes
+        unsigned mx = 0, mb = 0, mc = 0;
 #pragma unroll
-        for (int i = lane; i < TC * CH / 4; i += 32) bad |= out_of_range4(reinterpret_cast<const int4*>(&st.x[0][0])[i]);
+        for (int i = lane; i < TC * CH / 4; i += 32) {
+            const int4 v = reinterpret_cast<const int4*>(&st.x[0][0])[i];
+            bad |= out_of_range4(v);
+            mx = max(mx, absmax4(v));
+        }
 #pragma unroll
-        for (int i = lane; i < TC * 2 * NS / 4; i += 32)
-            bad |= out_of_range4(reinterpret_cast<const int4*>(&st.bc[0][0])[i]);
+        for (int i = lane; i < TC * 2 * NS / 4; i += 32) {  // 8 int4 per row: B in 0..3, C in 4..7
+            const int4 v = reinterpret_cast<const int4*>(&st.bc[0][0])[i];
+            bad |= out_of_range4(v);
+            if ((i & 7) < 4) mb = max(mb, absmax4(v));
+            else mc = max(mc, absmax4(v));
+        }
+        unsigned hm = 0;
+#pragma unroll
+        for (int j = 0; j < SPL; j++) hm = max(hm, uabs(h[j]));
+        mx = __reduce_max_sync(0xffffffffu, mx);
+        mb = __reduce_max_sync(0xffffffffu, mb);
+        mc = __reduce_max_sync(0xffffffffu, mc);
+        hm = __reduce_max_sync(0xffffffffu, hm);
+        // |h| grows by at most |B*x| per step (|floor(h*n/2^k)| <= |h|), so over the
+        // chunk every state stays within hb and every partial y sum within NS*|C|*hb
+        bool fast = mx <= 32767u && mb <= 32767u && mc <= 32767u;
+        if (fast) {
+            const unsigned long long hb = (unsigned long long)hm + (unsigned long long)TC * mb * mx;
+            fast = hb <= (unsigned long long)INT32_MAX && (unsigned long long)NS * mc * hb <= (unsigned long long)INT32_MAX;
+        }
         const int t0 = c * TC;
         const int tn = min(TC, L - t0);
-#pragma unroll 2
-        for (int r = 0; r < tn; r++) {
-            const int32_t xv = st.x[r][ch];
-            int32_t bb[SPL], cc[SPL];
-#pragma unroll
-            for (int q = 0; q < SPL / 4; q++) {
-                const int4 b4 = *reinterpret_cast<const int4*>(&st.bc[r][sub * SPL + 4 * q]);
-                const int4 c4 = *reinterpret_cast<const int4*>(&st.bc[r][NS + sub * SPL + 4 * q]);
-                bb[4 * q] = b4.x; bb[4 * q + 1] = b4.y; bb[4 * q + 2] = b4.z; bb[4 * q + 3] = b4.w;
-                cc[4 * q] = c4.x; cc[4 * q + 1] = c4.y; cc[4 * q + 2] = c4.z; cc[4 * q + 3] = c4.w;
-            }
-            // two independent 64-bit multiply-add chains for y (integer sums are
-            // exact in any order)
-            long long acc0 = 0, acc1 = 0;
-            int32_t ovl = 0;
-#pragma unroll
-            for (int j = 0; j < SPL; j++) {
-                const long long p = (long long)h[j] * (long long)nn[j];
-                const int32_t s = (int32_t)(p >> k);
-                const int32_t bx = (int32_t)((uint32_t)bb[j] * (uint32_t)xv);  // |B*x| < 2^30 when in range
-                const int32_t hn = (int32_t)((uint32_t)s + (uint32_t)bx);
-                ovl |= (s ^ hn) & (bx ^ hn);
-                h[j] = hn;
-                if (j & 1) acc1 += (long long)cc[j] * (long long)hn;
-                else acc0 += (long long)cc[j] * (long long)hn;
-            }
-            ovf |= ovl;
-            long long acc = acc0 + acc1;
-#pragma unroll
-            for (int o = 1; o < LPC; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-            if (sub == 0) ys[r][ch] = acc;
-        }
+        if (fast)
+            scan_chunk<LPC, true, CH, P>(h, nm, am, st, ys, tn, ch, sub, ovf);
+        else
+            scan_chunk<LPC, false, CH, P>(h, nm, am, st, ys, tn, ch, sub, ovf);
         __syncwarp();
         // write the chunk's y rows: TC rows x CH values as 16-byte vectors
         if (Y64) {
@@ -181,7 +263,13 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
                 const int dq = d0 + 2 * q;
                 if (r < tn && dq < D) {
                     int64_t* o = y64 + (row0 + t0 + r) * D + dq;
-                    *reinterpret_cast<longlong2*>(o) = make_longlong2(ys[r][2 * q], ys[r][2 * q + 1]);
+                    long long a0 = 0, a1 = 0;
+#pragma unroll
+                    for (int p = 0; p < P; p++) {
+                        a0 += ys[r][(2 * q) * P + p];
+                        a1 += ys[r][(2 * q + 1) * P + p];
+                    }
+                    *reinterpret_cast<longlong2*>(o) = make_longlong2(a0, a1);
                 }
             }
         } else {
@@ -193,7 +281,9 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
                     int32_t v[4];
 #pragma unroll
                     for (int e = 0; e < 4; e++) {
-                        const long long a = ys[r][4 * q + e];
+                        long long a = 0;
+#pragma unroll
+                        for (int p = 0; p < P; p++) a += ys[r][(4 * q + e) * P + p];
                         if (a > INT32_MAX || a < INT32_MIN) ovf |= INT32_MIN;
                         v[e] = (int32_t)a;
                     }

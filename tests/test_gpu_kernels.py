@@ -65,6 +65,47 @@ def test_scan_i32_full_input_range(cuda_dev, bsz, D):
     _eq(h64, h_ref, "h")
 
 
+@pytest.mark.parametrize("kk", [1, 7, 15, 30])
+def test_scan_i32_shift_amounts(cuda_dev, kk):
+    """Every k the API takes, with n at 0, 2^(k-1)-1, 2^(k-1) and 2^k (where the
+    kernel's multiply-high form of (h*n) >> k changes case) and large states."""
+    k = _mi()
+    bsz, L, D = 2, 100, 64
+    g = torch.Generator().manual_seed(kk)
+    q = lambda *s: torch.round(torch.randn(*s, generator=g) * 32).clamp(-127, 127).to(torch.int32)  # noqa: E731
+    x, B, C = q(bsz, L, D), q(bsz, L, 16), q(bsz, L, 16)
+    n = torch.randint(0, 2 ** kk + 1, (D, 16), generator=g, dtype=torch.int32)
+    n[0, :4] = torch.tensor([0, max(2 ** (kk - 1) - 1, 0), 2 ** (kk - 1), 2 ** kk])
+    h0 = torch.randint(-2 ** 28, 2 ** 28, (bsz, D, 16), generator=g, dtype=torch.int32)
+    y_ref, h_ref = orc.scan_i32(x.numpy(), B.numpy(), C.numpy(), n.numpy(), kk, h0=h0.numpy())
+    y64, h64 = k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), kk, h0=h0.to(cuda_dev), y_dtype=torch.int64)
+    _eq(y64, y_ref, "y64")
+    _eq(h64, h_ref, "h")
+
+
+@pytest.mark.parametrize("y_dtype", [torch.int64, torch.int32])
+def test_scan_i32_chunk_paths_switch(cuda_dev, y_dtype):
+    """Large initial states (chunks whose bound does not rule out an int32
+    overflow: 64-bit y sums, checked adds) that decay within a few chunks to
+    states where the 32-bit path applies; one sequence crosses over."""
+    k = _mi()
+    bsz, L, D = 3, 400, 96
+    g = torch.Generator().manual_seed(77)
+    q = lambda *s: torch.round(torch.randn(*s, generator=g) * 32).clamp(-127, 127).to(torch.int32)  # noqa: E731
+    x, B, C = q(bsz, L, D), q(bsz, L, 16), q(bsz, L, 16)
+    n = torch.randint(0, 2 ** 14 + 1, (D, 16), generator=g, dtype=torch.int32)  # decay <= 1/2
+    hbits = 30 if y_dtype == torch.int64 else 21  # int32 y: 16 * 127 * 2^21 > 2^31 still needs the wide path
+    h0 = torch.randint(-2 ** hbits, 2 ** hbits, (bsz, D, 16), generator=g, dtype=torch.int32)
+    h0[1] = 0  # this sequence starts small
+    y_ref, h_ref = orc.scan_i32(x.numpy(), B.numpy(), C.numpy(), n.numpy(), 15, h0=h0.numpy())
+    if y_dtype == torch.int32:
+        assert np.abs(y_ref).max() < 2 ** 31
+        y_ref = y_ref.astype(np.int32)
+    y, h = k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), 15, h0=h0.to(cuda_dev), y_dtype=y_dtype)
+    _eq(y, y_ref, "y")
+    _eq(h, h_ref, "h")
+
+
 def test_scan_i32_kat_negative_floor(cuda_dev):
     """h = -1, n = 1, k = 15: (-1*1) >> 15 = -1 (floor), not 0 (truncation)."""
     k = _mi()
