@@ -18,10 +18,11 @@
 // barriers).  A full chunk runs as one unrolled block, so that the loads and
 // y sums of a step overlap the state chains of the next ones (the kernel is
 // bound by dependency latency: few warps per SM, each a serial recurrence).
-// Each lane's partial y sum is staged in shared memory; the writer adds the
-// LPC partials of a channel and stores 16-byte vectors.  LPC = 2 at config 2
-// sizes: the B|C values every lane must receive each step share the
-// load/store data path, which fewer lanes per channel use less of.
+// The LPC partial y sums of a channel meet in shuffles and each step's y
+// row segment (CH consecutive channels) is stored at once, with no staging.
+// LPC = 2 at config 2 sizes: the B|C values every lane must receive each
+// step share the load/store data path, which fewer lanes per channel use
+// less of.
 //
 // Exactness: the shifted product fits int32 whenever 0 <= n <= 2^k, and its
 // magnitude never exceeds |h|; |B*x| < 2^30 when |B|,|x| <= 32767.  Per chunk,
@@ -48,7 +49,6 @@ struct Geo {
     static constexpr int SPL = NS / LPC;  // states per lane
     static constexpr int CH = 32 / LPC;   // channels per warp
     static constexpr int XQ = CH / 4;     // 16-byte chunks per staged x row
-    static constexpr int P = LPC < 2 ? LPC : 2;  // partial y sums staged per channel
 };
 
 template <int CH>
@@ -89,25 +89,27 @@ __device__ __forceinline__ void load_chunk(Stage<CH>& st, int t0, const int32_t*
     }
 }
 
-// One time step of one lane's SPL states; its partial y sum goes to ys_row
-// (P partials per channel, summed by the writer: no shuffle on the step's
-// path except one for 4 lanes per channel).
+// One time step of one lane's SPL states.  The LPC partial y sums of a
+// channel meet in shuffles and the channel's first lane stores y to `yout`
+// (a warp stores CH consecutive values of the row in one instruction).
 //
 // The shifted product floor(h * n / 2^k) is the high word of h * (n * 2^(32-k)):
 // with m = n << (32 - k) taken as a signed int32, mul.hi gives
 // floor(h * m / 2^32), which is 2^32 * h too small exactly when n * 2^(32-k)
 // >= 2^31 (m wrapped negative, or to 0 for n = 2^k), so the lane adds h there
-// (am = -1 selects it).  0 <= n <= 2^k keeps |result| <= |h|.
+// (am = -1 selects it).  0 <= n <= 2^k keeps |result| <= |h|.  AMALL: every
+// n of the warp is >= 2^(k-1), so h is added back unconditionally (the add
+// folds into the multiply-high).
 //
 // FAST: the chunk's bound (checked by the caller) rules out every int32
 // overflow of the states and of 32-bit y sums, so neither is tested or
 // widened.  Otherwise the y sums are 64-bit and each state add is checked.
-template <int LPC, bool FAST>
+template <int LPC, bool FAST, bool AMALL, typename Out>
 __device__ __forceinline__ void scan_step(int32_t (&h)[Geo<LPC>::SPL], const int32_t (&nm)[Geo<LPC>::SPL],
                                           const int32_t (&am)[Geo<LPC>::SPL], int32_t xv,
-                                          const int32_t* __restrict__ bc_row, int ch, int sub,
-                                          int64_t* __restrict__ ys_row, int32_t& ovf) {
-    constexpr int SPL = Geo<LPC>::SPL, P = Geo<LPC>::P;
+                                          const int32_t* __restrict__ bc_row, int sub, Out* __restrict__ yout,
+                                          bool store, int32_t& ovf) {
+    constexpr int SPL = Geo<LPC>::SPL;
     constexpr int NACC = SPL < 4 ? SPL : 4;  // independent multiply-add chains for y
     int32_t bb[SPL], cc[SPL];
 #pragma unroll
@@ -125,7 +127,7 @@ __device__ __forceinline__ void scan_step(int32_t (&h)[Geo<LPC>::SPL], const int
     int32_t ovl = 0;
 #pragma unroll
     for (int j = 0; j < SPL; j++) {
-        const int32_t s = __mulhi(h[j], nm[j]) + (h[j] & am[j]);
+        const int32_t s = __mulhi(h[j], nm[j]) + (AMALL ? h[j] : (h[j] & am[j]));
         const int32_t bx = (int32_t)((uint32_t)bb[j] * (uint32_t)xv);  // |B*x| < 2^30 when in range
         const int32_t hn = (int32_t)((uint32_t)s + (uint32_t)bx);
         if (!FAST) ovl |= (s ^ hn) & (bx ^ hn);
@@ -137,15 +139,13 @@ __device__ __forceinline__ void scan_step(int32_t (&h)[Geo<LPC>::SPL], const int
     for (int w = NACC / 2; w >= 1; w /= 2)
 #pragma unroll
         for (int a = 0; a < w; a++) acc[a] += acc[a + w];
-    long long y = acc[0];
-    if (LPC == 4) y += __shfl_xor_sync(0xffffffffu, y, 1);
-    if (LPC != 4 || (sub & 1) == 0) ys_row[ch * P + (LPC == 4 ? sub >> 1 : sub)] = y;
-}
-
-__device__ __forceinline__ int out_of_range4(int4 v) {
-    // |v| > 32767 for any component (the preconditions of the exact int32 path)
-    return ((unsigned)v.x + 32767u > 65534u) | ((unsigned)v.y + 32767u > 65534u) |
-           ((unsigned)v.z + 32767u > 65534u) | ((unsigned)v.w + 32767u > 65534u);
+    Acc y = acc[0];
+#pragma unroll
+    for (int o = 1; o < LPC; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
+    if (store) {
+        if (sizeof(Out) == 4 && !FAST && ((long long)y > INT32_MAX || (long long)y < INT32_MIN)) ovf |= INT32_MIN;
+        *yout = (Out)y;
+    }
 }
 
 __device__ __forceinline__ unsigned uabs(int32_t v) {
@@ -156,19 +156,21 @@ __device__ __forceinline__ unsigned absmax4(int4 v) {
     return max(max(uabs(v.x), uabs(v.y)), max(uabs(v.z), uabs(v.w)));
 }
 
-// The steps of one staged chunk (tn of them).
-template <int LPC, bool FAST, int CH, int P>
+// The steps of one staged chunk (tn of them); y of step r goes to yb + r * D.
+template <int LPC, bool FAST, bool AMALL, int CH, typename Out>
 __device__ __forceinline__ void scan_chunk(int32_t (&h)[Geo<LPC>::SPL], const int32_t (&nm)[Geo<LPC>::SPL],
-                                           const int32_t (&am)[Geo<LPC>::SPL], const Stage<CH>& st,
-                                           int64_t (&ys)[TC][CH * P], int tn, int ch, int sub, int32_t& ovf) {
+                                           const int32_t (&am)[Geo<LPC>::SPL], const Stage<CH>& st, Out* yb,
+                                           int D, bool store, int tn, int ch, int sub, int32_t& ovf) {
     if (tn == TC) {
-        // a full chunk as one straight-line block: the steps' loads and y sums
-        // overlap the state chains of the following steps
+        // a full chunk as one straight-line block: the steps' loads, y sums and
+        // stores overlap the state chains of the following steps
 #pragma unroll
-        for (int r = 0; r < TC; r++) scan_step<LPC, FAST>(h, nm, am, st.x[r][ch], st.bc[r], ch, sub, ys[r], ovf);
+        for (int r = 0; r < TC; r++)
+            scan_step<LPC, FAST, AMALL>(h, nm, am, st.x[r][ch], st.bc[r], sub, yb + (size_t)r * D, store, ovf);
     } else {
 #pragma unroll 1
-        for (int r = 0; r < tn; r++) scan_step<LPC, FAST>(h, nm, am, st.x[r][ch], st.bc[r], ch, sub, ys[r], ovf);
+        for (int r = 0; r < tn; r++)
+            scan_step<LPC, FAST, AMALL>(h, nm, am, st.x[r][ch], st.bc[r], sub, yb + (size_t)r * D, store, ovf);
     }
 }
 
@@ -178,9 +180,8 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
                 const int32_t* __restrict__ n, const int k, int32_t* __restrict__ y32, int64_t* __restrict__ y64,
                 int32_t* __restrict__ h_io, int L, int D) {
     using G = Geo<LPC>;
-    constexpr int SPL = G::SPL, CH = G::CH, P = G::P;
+    constexpr int SPL = G::SPL, CH = G::CH;
     __shared__ __align__(16) Stage<CH> stage[SST];
-    __shared__ __align__(16) int64_t ys[TC][CH * P];  // partial y sums of the chunk
     const int lane = threadIdx.x;
     const int b = blockIdx.y;
     const int d0 = blockIdx.x * CH;
@@ -188,6 +189,7 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
     const int sub = lane % LPC;  // which SPL states
     const int d = d0 + ch;
     const bool active = d < D;
+    const bool store = active && sub == 0;
     const size_t row0 = (size_t)b * L;
 
     // states, and each n as the multiplier n << (32 - k) and the add-back mask
@@ -203,6 +205,10 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
         nm[j] = (int32_t)((uint32_t)nv << (32 - k));
         am[j] = (nv >= (lim >> 1)) ? -1 : 0;
     }
+    int lane_amall = 1;
+#pragma unroll
+    for (int j = 0; j < SPL; j++) lane_amall &= (am[j] == -1);
+    const bool amall = __all_sync(0xffffffffu, lane_amall);
 
     int ovf = 0;  // sign-test accumulator: negative => an int32 state or y32 overflowed
     const int nchunks = cdiv(L, TC);
@@ -219,20 +225,16 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
         asm volatile("cp.async.commit_group;\n" ::: "memory");
         asm volatile("cp.async.wait_group %0;\n" ::"n"(SST - 1) : "memory");
         __syncwarp();
-        // range check of the staged inputs, and their largest magnitudes
+        // the staged inputs' largest magnitudes (range check and chunk bound)
         unsigned mx = 0, mb = 0, mc = 0;
 #pragma unroll
-        for (int i = lane; i < TC * CH / 4; i += 32) {
-            const int4 v = reinterpret_cast<const int4*>(&st.x[0][0])[i];
-            bad |= out_of_range4(v);
-            mx = max(mx, absmax4(v));
-        }
+        for (int i = lane; i < TC * CH / 4; i += 32)
+            mx = max(mx, absmax4(reinterpret_cast<const int4*>(&st.x[0][0])[i]));
 #pragma unroll
         for (int i = lane; i < TC * 2 * NS / 4; i += 32) {  // 8 int4 per row: B in 0..3, C in 4..7
-            const int4 v = reinterpret_cast<const int4*>(&st.bc[0][0])[i];
-            bad |= out_of_range4(v);
-            if ((i & 7) < 4) mb = max(mb, absmax4(v));
-            else mc = max(mc, absmax4(v));
+            const unsigned m = absmax4(reinterpret_cast<const int4*>(&st.bc[0][0])[i]);
+            if ((i & 7) < 4) mb = max(mb, m);
+            else mc = max(mc, m);
         }
         unsigned hm = 0;
 #pragma unroll
@@ -244,54 +246,30 @@ scan_i32_kernel(const int32_t* __restrict__ x, const int32_t* __restrict__ Bm, c
         // |h| grows by at most |B*x| per step (|floor(h*n/2^k)| <= |h|), so over the
         // chunk every state stays within hb and every partial y sum within NS*|C|*hb
         bool fast = mx <= 32767u && mb <= 32767u && mc <= 32767u;
+        bad |= !fast;  // |x|, |B| or |C| above 32767
         if (fast) {
             const unsigned long long hb = (unsigned long long)hm + (unsigned long long)TC * mb * mx;
             fast = hb <= (unsigned long long)INT32_MAX && (unsigned long long)NS * mc * hb <= (unsigned long long)INT32_MAX;
         }
         const int t0 = c * TC;
         const int tn = min(TC, L - t0);
-        if (fast)
-            scan_chunk<LPC, true, CH, P>(h, nm, am, st, ys, tn, ch, sub, ovf);
-        else
-            scan_chunk<LPC, false, CH, P>(h, nm, am, st, ys, tn, ch, sub, ovf);
-        __syncwarp();
-        // write the chunk's y rows: TC rows x CH values as 16-byte vectors
+        const size_t yoff = (row0 + t0) * D + (active ? d : 0);
         if (Y64) {
-#pragma unroll
-            for (int i = lane; i < TC * (CH / 2); i += 32) {
-                const int r = i / (CH / 2), q = i % (CH / 2);  // chunks of two int64 per row
-                const int dq = d0 + 2 * q;
-                if (r < tn && dq < D) {
-                    int64_t* o = y64 + (row0 + t0 + r) * D + dq;
-                    long long a0 = 0, a1 = 0;
-#pragma unroll
-                    for (int p = 0; p < P; p++) {
-                        a0 += ys[r][(2 * q) * P + p];
-                        a1 += ys[r][(2 * q + 1) * P + p];
-                    }
-                    *reinterpret_cast<longlong2*>(o) = make_longlong2(a0, a1);
-                }
-            }
+            if (fast && amall)
+                scan_chunk<LPC, true, true, CH>(h, nm, am, st, y64 + yoff, D, store, tn, ch, sub, ovf);
+            else if (fast)
+                scan_chunk<LPC, true, false, CH>(h, nm, am, st, y64 + yoff, D, store, tn, ch, sub, ovf);
+            else
+                scan_chunk<LPC, false, false, CH>(h, nm, am, st, y64 + yoff, D, store, tn, ch, sub, ovf);
         } else {
-#pragma unroll
-            for (int i = lane; i < TC * (CH / 4); i += 32) {
-                const int r = i / (CH / 4), q = i % (CH / 4);  // chunks of four int32 per row
-                const int dq = d0 + 4 * q;
-                if (r < tn && dq < D) {
-                    int32_t v[4];
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        long long a = 0;
-#pragma unroll
-                        for (int p = 0; p < P; p++) a += ys[r][(4 * q + e) * P + p];
-                        if (a > INT32_MAX || a < INT32_MIN) ovf |= INT32_MIN;
-                        v[e] = (int32_t)a;
-                    }
-                    *reinterpret_cast<int4*>(y32 + (row0 + t0 + r) * D + dq) = make_int4(v[0], v[1], v[2], v[3]);
-                }
-            }
+            if (fast && amall)
+                scan_chunk<LPC, true, true, CH>(h, nm, am, st, y32 + yoff, D, store, tn, ch, sub, ovf);
+            else if (fast)
+                scan_chunk<LPC, true, false, CH>(h, nm, am, st, y32 + yoff, D, store, tn, ch, sub, ovf);
+            else
+                scan_chunk<LPC, false, false, CH>(h, nm, am, st, y32 + yoff, D, store, tn, ch, sub, ovf);
         }
-        __syncwarp();  // ys and the stage slot are rewritten in the next iterations
+        __syncwarp();  // the stage slot is refilled by the next iteration
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 
