@@ -65,6 +65,23 @@ def test_scan_i32_full_input_range(cuda_dev, bsz, D):
     _eq(h64, h_ref, "h")
 
 
+def test_scan_i32_config2_distribution(cuda_dev):
+    """Config 2's input distribution at a reduced size from zero states: every
+    chunk takes the 32-bit path, and every warp but channel 0's has all decays
+    >= 2^(k-1) (the folded add-back)."""
+    k = _mi()
+    bsz, L, D = 2, 512, 256
+    g = torch.Generator().manual_seed(5)
+    q = lambda *s: torch.round(torch.randn(*s, generator=g) * 32).clamp(-127, 127).to(torch.int32)  # noqa: E731
+    x, B, C = q(bsz, L, D), q(bsz, L, 16), q(bsz, L, 16)
+    n = torch.randint(int(0.90 * 2 ** 15), int(0.999 * 2 ** 15) + 1, (D, 16), generator=g, dtype=torch.int32)
+    n[0, 5] = 2 ** 14 - 1
+    y_ref, h_ref = orc.scan_i32(x.numpy(), B.numpy(), C.numpy(), n.numpy(), 15)
+    y, h = k.scan_i32(*(t.to(cuda_dev) for t in (x, B, C, n)), 15, y_dtype=torch.int32)
+    _eq(y, y_ref.astype(np.int32), "y32")
+    _eq(h, h_ref, "h")
+
+
 @pytest.mark.parametrize("kk", [1, 7, 15, 30])
 def test_scan_i32_shift_amounts(cuda_dev, kk):
     """Every k the API takes, with n at 0, 2^(k-1)-1, 2^(k-1) and 2^k (where the
