@@ -454,7 +454,24 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
             }
         }
         __syncwarp();
-        // (B) the recurrence, one step at a time
+        // (B) the recurrence, one step at a time.  A full chunk whose steps all
+        // take the fast path runs as one branch-free block (the loads of later
+        // steps and the h.C chains of earlier ones overlap); otherwise step by step.
+        if (S == 1 && tn == SC && fast_mask == (1u << SC) - 1) {
+#pragma unroll
+            for (int j = 0; j < SC; j++) {
+                const float ms = __fmul_rn(st.mod[j][ch], 3.0517578125e-05f);
+                const float xdt = st.act[j][ch];
+#pragma unroll
+                for (int i = 0; i < NSL; i += 2)
+                    state_pair_fast(h[i], h[i + 1], bsl[i], bsl[i + 1], make_float2(ms, ms), make_float2(xdt, xdt),
+                                    st.bc[j][i], st.bc[j][i + 1]);
+                float yacc = 0.0f;
+#pragma unroll
+                for (int i = 0; i < NSL; i++) yacc = __fmaf_rn(h[i], st.bc[j][NS + i], yacc);
+                st.mod[j][ch] = yacc;
+            }
+        } else
 #pragma unroll 1
         for (int j = 0; j < tn; j++) {
             const float mod = st.mod[j][ch];
@@ -695,7 +712,27 @@ ssm_scan_split_kernel(const float* __restrict__ act, const float* __restrict__ b
             }
         }
         __syncwarp();
-        // (B1) state recurrence; snapshot of every step
+        // (B1) state recurrence; snapshot of every step (a full all-fast chunk as
+        // one branch-free block, as in the one-lane kernel)
+        if (tn == SC && fast_mask == (1u << SC) - 1) {
+#pragma unroll
+            for (int j = 0; j < SC; j++) {
+                const float ms = __fmul_rn(st.mod[j][ch], 3.0517578125e-05f);
+                const float xdt = st.act[j][ch];
+                const float* Bv = &st.bc[j][sub * NSL];
+#pragma unroll
+                for (int i = 0; i < NSL; i += 2)
+                    state_pair_fast(h[i], h[i + 1], bsl[i], bsl[i + 1], make_float2(ms, ms), make_float2(xdt, xdt),
+                                    Bv[i], Bv[i + 1]);
+                if (NSL % 4 == 0) {
+#pragma unroll
+                    for (int i = 0; i < NSL; i += 4)
+                        *reinterpret_cast<float4*>(&snap[j][lane][i]) = make_float4(h[i], h[i + 1], h[i + 2], h[i + 3]);
+                } else {
+                    *reinterpret_cast<float2*>(&snap[j][lane][0]) = make_float2(h[0], h[1]);
+                }
+            }
+        } else
 #pragma unroll 1
         for (int j = 0; j < tn; j++) {
             const float mod = st.mod[j][ch];
