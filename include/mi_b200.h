@@ -203,8 +203,10 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * w_dt int8 [D, ceil16(R)] (zero-padded) and w_dt_scale [1]; each channel
  * forms the exact int32 dot product and the BitLinear rescale
  * acc * (w_dt_scale * dts[t]) itself.  R <= 64.
- * split = lanes per channel (1, 2, 4 or 8; 0 = chosen from batch*D vs the SM
- * count): more lanes per channel keep small per-GPU batches occupied.
+ * split = kernel variant: 1, 2, 4 or 8 lanes per channel, or 3 = one lane per
+ * channel with the chunk's phases pipelined over three warps (staging and
+ * decay, recurrence, gate); 0 = chosen from batch*D vs the SM count (1 when
+ * the layer fills the GPU, else 3).  All variants give identical results.
  * h_out (optional, [batch, D, N], 16-byte aligned) receives the states after
  * the last position (the starting point of mi_ssm_step).
  * Replaces: dt_proj + DyadicScanFunction section, src/mamba_integer_model.py:419-444

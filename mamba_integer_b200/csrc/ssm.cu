@@ -565,6 +565,237 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
     }
 }
 
+// Three-warp pipeline for small per-GPU batches (few warps per SM, where the
+// one-warp kernels above spend most of each chunk waiting on their own
+// phases in series).  One CTA owns 32 channels of one sequence, one lane per
+// channel as in ssm_scan_kernel<RW, 1>, and splits the chunk's phases over
+// three warps that work on different chunks at once:
+//   warp 0 stages chunk c + WS3_LA by cp.async and runs phase A (decay_mod,
+//          dt, x*dt, fast-path vote) of chunk c;
+//   warp 1 runs the recurrence and the h.C contraction of chunk c - 1;
+//   warp 2 gates, stores and reduces the row absmax of chunk c - 2.
+// Chunks pass through a ring of WS3_NR staging slots; each slot has three
+// named barriers (phase A done -> recurrence, recurrence done -> gate, gate
+// done -> restaging), each completed by one arriving and one waiting warp.
+// Every warp takes every chunk in order, so each arrival has exactly one
+// matching wait (the gate warp signals a slot only when the staging warp
+// will refill it).  The arithmetic is that of ssm_scan_kernel<RW, 1>.
+constexpr int WS3_NR = 5;  // ring slots
+constexpr int WS3_LA = 2;  // chunks staged ahead of the one in phase A
+
+__device__ __forceinline__ void named_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+template <int RW>
+__global__ void __launch_bounds__(96)
+ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
+                    const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
+                    float* __restrict__ amax, float* __restrict__ h_out, int L, int D) {
+    static_assert(WS3_LA <= WS3_NR - 3, "the ring holds a slot in each phase plus the staged ones");
+    static_assert(3 * WS3_NR + 1 <= 16, "named barrier ids");
+    __shared__ __align__(16) ScanStage ring[WS3_NR];
+    __shared__ unsigned fmask[WS3_NR];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.y;
+    const int d0 = blockIdx.x * 32;
+    const int d = d0 + lane;
+    const bool active = d < D;
+    const int dd = active ? d : 0;
+    const size_t row0 = (size_t)b * L;
+    const int nchunks = cdiv(L, SC);
+    constexpr int BA = 1, BB = 1 + WS3_NR, BG = 1 + 2 * WS3_NR;  // barrier id bases (0 is __syncthreads)
+    if (warp == 1) {
+        // ---- recurrence (same operations as ssm_scan_kernel<RW, 1>, phase B)
+        float h[NS], bsl[NS];
+#pragma unroll
+        for (int n = 0; n < NS; n++) {
+            bsl[n] = __fmul_rn(base[(size_t)dd * NS + n], 3.0517578125e-05f);
+            h[n] = 0.0f;
+        }
+        for (int c = 0; c < nchunks; c++) {
+            const int s = c % WS3_NR;
+            named_sync(BA + s, 64);
+            ScanStage& st = ring[s];
+            const unsigned fm = fmask[s];
+            const int tn = min(SC, L - c * SC);
+            if (tn == SC && fm == (1u << SC) - 1) {
+#pragma unroll
+                for (int j = 0; j < SC; j++) {
+                    const float ms = __fmul_rn(st.mod[j][lane], 3.0517578125e-05f);
+                    const float xdt = st.act[j][lane];
+#pragma unroll
+                    for (int i = 0; i < NS; i += 2)
+                        state_pair_fast(h[i], h[i + 1], bsl[i], bsl[i + 1], make_float2(ms, ms),
+                                        make_float2(xdt, xdt), st.bc[j][i], st.bc[j][i + 1]);
+                    float yacc = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < NS; i++) yacc = __fmaf_rn(h[i], st.bc[j][NS + i], yacc);
+                    st.mod[j][lane] = yacc;
+                }
+            } else {
+#pragma unroll 1
+                for (int j = 0; j < tn; j++) {
+                    const float mod = st.mod[j][lane];
+                    const float xdt = st.act[j][lane];
+                    if (fm & (1u << j)) {
+                        const float ms = __fmul_rn(mod, 3.0517578125e-05f);
+#pragma unroll
+                        for (int i = 0; i < NS; i += 2)
+                            state_pair_fast(h[i], h[i + 1], bsl[i], bsl[i + 1], make_float2(ms, ms),
+                                            make_float2(xdt, xdt), st.bc[j][i], st.bc[j][i + 1]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < NS; i++) {
+                            const float bn = __fmul_rn(bsl[i], 32768.0f);
+                            const float num = ste_clamp(__fadd_rn(bn, mod), 0.0f, 32000.0f);
+                            const float dec = __fmul_rn(num, 3.0517578125e-05f);
+                            const float u = __fmul_rn(xdt, st.bc[j][i]);
+                            h[i] = __fadd_rn(__fmul_rn(h[i], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));
+                        }
+                    }
+                    float yacc = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < NS; i++) yacc = __fmaf_rn(h[i], st.bc[j][NS + i], yacc);
+                    st.mod[j][lane] = yacc;
+                }
+            }
+            __syncwarp();
+            named_arrive(BB + s, 64);
+        }
+        if (h_out && active) {
+            float* dst = h_out + ((size_t)b * D + d) * NS;
+#pragma unroll
+            for (int i = 0; i < NS; i++) dst[i] = h[i];
+        }
+        return;
+    }
+    if (warp == 2) {
+        // ---- gate, store, row absmax (phase C of ssm_scan_kernel)
+        for (int c = 0; c < nchunks; c++) {
+            const int s = c % WS3_NR;
+            named_sync(BB + s, 64);
+            ScanStage& st = ring[s];
+            const int t0 = c * SC;
+            const int tn = min(SC, L - t0);
+            unsigned m[SC];
+#pragma unroll
+            for (int j = 0; j < SC; j++) {
+                const float out = sigmoid_gate(st.mod[j][lane], st.z[j][lane]);
+                if (j < tn && active) y[(row0 + t0 + j) * D + d] = out;
+                m[j] = (j < tn && active) ? __float_as_uint(fabsf(out)) : 0u;
+            }
+            __syncwarp();
+            if (c < nchunks - WS3_NR) named_arrive(BG + s, 64);  // the slot is restaged with chunk c + NR
+            if (amax) {
+                const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
+                unsigned m2[4], m3[2];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const unsigned send = b4 ? m[i] : m[4 + i], keep = b4 ? m[4 + i] : m[i];
+                    m2[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+                }
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const unsigned send = b3 ? m2[i] : m2[2 + i], keep = b3 ? m2[2 + i] : m2[i];
+                    m3[i] = max(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+                }
+                unsigned m4;
+                {
+                    const unsigned send = b2 ? m3[0] : m3[1], keep = b2 ? m3[1] : m3[0];
+                    m4 = max(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+                }
+                m4 = max(m4, __shfl_xor_sync(0xffffffffu, m4, 2));
+                m4 = max(m4, __shfl_xor_sync(0xffffffffu, m4, 1));
+                const int jstep = (b4 ? 4 : 0) + (b3 ? 2 : 0) + (b2 ? 1 : 0);
+                if ((lane & 3) == 0 && jstep < tn)
+                    atomicMax(reinterpret_cast<unsigned int*>(amax) + row0 + t0 + jstep, m4);
+            }
+        }
+        return;
+    }
+    // ---- staging and phase A (ssm_scan_kernel<RW, 1>, phase A)
+    int32_t wd[RW > 0 ? RW : 1];
+    float wsc = 0.0f;
+    if (RW > 0) {
+        const int4* wrow = reinterpret_cast<const int4*>(src.w + (size_t)dd * (4 * RW));
+#pragma unroll
+        for (int k = 0; k < RW / 4; k++) {
+            const int4 v = wrow[k];
+            wd[4 * k] = v.x; wd[4 * k + 1] = v.y; wd[4 * k + 2] = v.z; wd[4 * k + 3] = v.w;
+        }
+        wsc = *src.w_scale;
+    }
+    float bmin = __int_as_float(0x7f800000), bmax = -__int_as_float(0x7f800000);
+    bool bnan = false;
+#pragma unroll
+    for (int n = 0; n < NS; n++) {
+        const float bv = base[(size_t)dd * NS + n];
+        bmin = fminf(bmin, bv);
+        bmax = fmaxf(bmax, bv);
+        bnan |= (bv != bv);
+    }
+    const bool wide_ok = !bnan && (bmin >= 37.0f) && (bmax <= 63963.0f);  // see ssm_scan_kernel
+#pragma unroll
+    for (int c = 0; c < WS3_LA; c++) {
+        if (c < nchunks) scan_stage_load<RW, 32>(ring[c], act, src, z, bc, ldbc, ldz, row0, c * SC, L, d0, D);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    }
+    for (int c = 0; c < nchunks; c++) {
+        const int cn = c + WS3_LA;
+        if (cn < nchunks) {
+            const int sn = cn % WS3_NR;
+            if (cn >= WS3_NR) named_sync(BG + sn, 64);  // the gate warp is done with chunk cn - NR
+            scan_stage_load<RW, 32>(ring[sn], act, src, z, bc, ldbc, ldz, row0, cn * SC, L, d0, D);
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(WS3_LA) : "memory");
+        __syncwarp();
+        const int s = c % WS3_NR;
+        ScanStage& st = ring[s];
+        float modr[SC];
+        if (RW > 0) {
+#pragma unroll
+            for (int j = 0; j < SC; j++) {
+                const int4* q4 = reinterpret_cast<const int4*>(&st.dtq[j][0]);
+                int acc0 = 0, acc1 = 0;  // exact: integer sums in any order
+#pragma unroll
+                for (int k = 0; k < RW / 4; k++) {
+                    const int4 qv = q4[k];
+                    acc0 = __dp4a(qv.x, wd[4 * k], acc0);
+                    acc1 = __dp4a(qv.y, wd[4 * k + 1], acc1);
+                    acc0 = __dp4a(qv.z, wd[4 * k + 2], acc0);
+                    acc1 = __dp4a(qv.w, wd[4 * k + 3], acc1);
+                }
+                modr[j] = __fmul_rn((float)(acc0 + acc1), __fmul_rn(wsc, st.dts[j]));
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < SC; j++) modr[j] = st.mod[j][lane];
+        }
+        unsigned fast_mask = 0;
+#pragma unroll
+        for (int j = 0; j < SC; j++) {
+            const float mod = ste_clamp(modr[j], -20.0f, 20.0f);
+            const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);
+            bool inside = (mod == 0.0f || fabsf(mod) >= 1e-30f);
+            if (!wide_ok)
+                inside = inside && !bnan && (bmin >= 1.0f) && (__fadd_rn(bmin, mod) >= 0.0f) &&
+                         (__fadd_rn(bmax, mod) <= 64000.0f);
+            if (__all_sync(0xffffffffu, inside)) fast_mask |= 1u << j;
+            st.mod[j][lane] = mod;
+            st.act[j][lane] = __fmul_rn(st.act[j][lane], dtv);  // x * dt_val
+        }
+        if (lane == 0) fmask[s] = fast_mask;
+        __syncwarp();
+        named_arrive(BA + s, 64);
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
 // ---------------------------------------------------------------------------
 // stand-alone convex scan and element-wise ops
 // ---------------------------------------------------------------------------
@@ -870,8 +1101,10 @@ extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, 
 namespace mi {
 namespace ssm {
 
-// Lanes per channel: 1 when the layer's (sequence, channel) pairs give at
-// least 8 warps per SM, else 2 or 4 (small per-GPU batches).
+// Kernel choice: one lane per channel (ssm_scan_kernel) when the layer's
+// (sequence, 32-channel) groups give at least 8 warps per SM; below that the
+// three-warp pipeline (ssm_scan_ws3_kernel).  2, 4 or 8 lanes per channel
+// (ssm_scan_split_kernel) stay available by explicit request.
 static int pick_split(int batch, int D) {
     static int sms = 0;
     if (!sms) {
@@ -881,15 +1114,20 @@ static int pick_split(int batch, int D) {
         if (sms <= 0) sms = 148;
     }
     const long long want = 8LL * sms;
-    if ((long long)batch * cdiv(D, 32) >= want) return 1;
-    if ((long long)batch * cdiv(D, 16) >= want) return 2;
-    return 4;
+    const long long units = (long long)batch * cdiv(D, 32);  // (sequence, 32-channel group) pairs
+    if (units >= want) return 1;
+    return 3;  // the three-warp pipeline (measured faster than 2 or 4 lanes per channel there)
 }
 
 template <int RW>
 static void launch_scan(int split, int batch, int L, int D, const float* act, const float* bc, int ldbc,
                         const DtSource& src, const float* z, int ldz, const float* base, float* y, float* amax,
                         float* h_out, cudaStream_t s) {
+    if (split == 3) {
+        dim3 grid(cdiv(D, 32), batch);
+        ssm_scan_ws3_kernel<RW><<<grid, 96, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
+        return;
+    }
     const int chw = SCAN_THREADS / split;
     dim3 grid(cdiv(D, chw), batch);
     if (split == 1)
@@ -931,7 +1169,7 @@ extern "C" int mi_ssm_scan_dt(const float* act, const float* bc, int ldbc, const
     if (!act || !bc || !dtq || !dts || !w_dt || !w_dt_scale || !z || !base || !y) return MI_ERR_INVALID;
     if (N != mi::ssm::NS) return MI_ERR_UNSUPPORTED;
     if (batch <= 0 || L <= 0 || D <= 0 || R <= 0 || ldbc < 2 * N || ldz < D) return MI_ERR_INVALID;
-    if (split != 0 && split != 1 && split != 2 && split != 4 && split != 8) return MI_ERR_INVALID;
+    if (split != 0 && split != 1 && split != 2 && split != 3 && split != 4 && split != 8) return MI_ERR_INVALID;
     const int R16 = (R + 15) / 16 * 16;
     if (R16 > 4 * mi::ssm::MAX_RW || ldq < R16 || (ldq & 15)) return MI_ERR_UNSUPPORTED;
     if (batch > 65535) return MI_ERR_UNSUPPORTED;

@@ -91,7 +91,7 @@ def test_prefill_final_states_match_oracle(cuda_dev):
     dtq_d = torch.zeros(bsz * L, 16, dtype=torch.int8)
     dtq_d[:, :R] = torch.from_numpy(dtq)
     h = torch.full((bsz, D, 16), float("nan"), device=cuda_dev)
-    for split in (1, 2, 4, 8):
+    for split in (1, 2, 3, 4, 8):
         y = kernels.ssm_scan_dt(dv(act), dv(bc), dv(dtq_d), dv(torch.from_numpy(dts)), dv(wdt),
                                 torch.tensor([ws], device=cuda_dev), R, dv(z), dv(base), bsz, L, split=split,
                                 h_out=h)
