@@ -376,7 +376,7 @@ def main():
     ap.add_argument("--batch", type=int, default=GLOBAL_BATCH)
     ap.add_argument("--seq", type=int, default=SEQ_LEN)
     ap.add_argument("--scan-split", type=int, default=0, choices=[0, 1, 2, 3, 4, 8],
-                    help="fused-scan variant: 1/2/4/8 lanes per channel, 3 = three-warp pipeline (0 = automatic)")
+                    help="fused-scan variant: 1/2/4/8 lanes per channel, 3 = pipelined (0 = automatic)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

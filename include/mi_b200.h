@@ -204,9 +204,9 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * forms the exact int32 dot product and the BitLinear rescale
  * acc * (w_dt_scale * dts[t]) itself.  R <= 64.
  * split = kernel variant: 1, 2, 4 or 8 lanes per channel, or 3 = one lane per
- * channel with the chunk's phases pipelined over three warps (staging and
- * decay, recurrence, gate); 0 = chosen from batch*D vs the SM count (1 when
- * the layer fills the GPU, else 3).  All variants give identical results.
+ * channel with each chunk's phases pipelined over four warps (two staging
+ * and decay, recurrence, gate); 0 = automatic (currently 3, the fastest at
+ * every measured batch).  All variants give identical results.
  * h_out (optional, [batch, D, N], 16-byte aligned) receives the states after
  * the last position (the starting point of mi_ssm_step).
  * Replaces: dt_proj + DyadicScanFunction section, src/mamba_integer_model.py:419-444

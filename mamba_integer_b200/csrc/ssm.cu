@@ -565,23 +565,29 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
     }
 }
 
-// Three-warp pipeline for small per-GPU batches (few warps per SM, where the
+// Pipelined kernel for small per-GPU batches (few warps per SM, where the
 // one-warp kernels above spend most of each chunk waiting on their own
 // phases in series).  One CTA owns 32 channels of one sequence, one lane per
-// channel as in ssm_scan_kernel<RW, 1>, and splits the chunk's phases over
-// three warps that work on different chunks at once:
-//   warp 0 stages chunk c + WS3_LA by cp.async and runs phase A (decay_mod,
-//          dt, x*dt, fast-path vote) of chunk c;
-//   warp 1 runs the recurrence and the h.C contraction of chunk c - 1;
-//   warp 2 gates, stores and reduces the row absmax of chunk c - 2.
-// Chunks pass through a ring of WS3_NR staging slots; each slot has three
-// named barriers (phase A done -> recurrence, recurrence done -> gate, gate
-// done -> restaging), each completed by one arriving and one waiting warp.
+// channel as in ssm_scan_kernel<RW, 1>, and splits each chunk's work over
+// four warps that work on different chunks at once:
+//   warps 0 and 1 stage rows 0-3 / 4-7 of chunk c + PIPE_LA by cp.async and
+//          run phase A (decay_mod, dt, x*dt, fast-path vote) of those rows
+//          of chunk c;
+//   warp 2 runs the recurrence and the h.C contraction of chunk c - 1;
+//   warp 3 gates, stores and reduces the row absmax of chunk c - 2.
+// Chunks pass through a ring of PIPE_NR staging slots; each slot has three
+// named barriers: phase A done (both staging warps arrive, the recurrence
+// warp waits), recurrence done (recurrence warp -> gate warp) and gate done
+// (gate warp arrives, both staging warps wait before restaging the slot).
 // Every warp takes every chunk in order, so each arrival has exactly one
-// matching wait (the gate warp signals a slot only when the staging warp
-// will refill it).  The arithmetic is that of ssm_scan_kernel<RW, 1>.
-constexpr int WS3_NR = 5;  // ring slots
-constexpr int WS3_LA = 2;  // chunks staged ahead of the one in phase A
+// matching wait (the gate warp signals a slot only when it will be
+// restaged), and a warp reaches a slot's barrier for chunk c + NR only after
+// the other warps have passed it for chunk c.  The arithmetic is that of
+// ssm_scan_kernel<RW, 1>.
+constexpr int PIPE_NR = 5;  // ring slots
+constexpr int PIPE_LA = 2;  // chunks staged ahead of the one in phase A
+static_assert(PIPE_LA <= PIPE_NR - 3, "the ring holds a slot in each phase plus the staged ones");
+static_assert(3 * PIPE_NR + 1 <= 16, "named barrier ids");
 
 __device__ __forceinline__ void named_arrive(int id, int n) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -590,15 +596,54 @@ __device__ __forceinline__ void named_sync(int id, int n) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
 
+// Stage rows 4*hf .. 4*hf+3 of chunk [t0, t0+SC) (32 channels) into `st`.
 template <int RW>
-__global__ void __launch_bounds__(96)
-ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
+__device__ __forceinline__ void stage_half(ScanStage& st, const float* __restrict__ act, const DtSource& src,
+                                           const float* __restrict__ z, const float* __restrict__ bc, int ldbc,
+                                           int ldz, size_t row0, int t0, int L, int d0, int D, int hf) {
+    const int lane = threadIdx.x & 31;
+    {   // act / z (/ mod): 4 rows x 8 chunks of 16 bytes
+        const int r = 4 * hf + (lane >> 3), q = lane & 7;
+        const int t = t0 + r;
+        const bool okt = t < L;
+        const bool ok = okt && (d0 + 4 * q < D);
+        const size_t row = row0 + (okt ? t : 0);
+        const int c = d0 + (ok ? 4 * q : 0);
+        cp_async16(&st.act[r][4 * q], act + row * D + c, ok);
+        if (RW == 0) cp_async16(&st.mod[r][4 * q], src.modraw + row * D + c, ok);
+        cp_async16(&st.z[r][4 * q], z + row * ldz + c, ok);
+    }
+    {   // B|C: 4 rows x 8 chunks
+        const int r = 4 * hf + (lane >> 3), q = lane & 7;
+        const int t = t0 + r;
+        const bool okt = t < L;
+        const size_t row = row0 + (okt ? t : 0);
+        cp_async16(&st.bc[r][4 * q], bc + row * ldbc + 4 * q, okt);
+    }
+    if (RW > 0) {
+        constexpr int RQ = RW > 0 ? RW / 4 : 1;
+        if (lane < 4 * RQ) {
+            const int r = 4 * hf + lane / RQ, q = lane % RQ;
+            const int t = t0 + r;
+            const bool okt = t < L;
+            const size_t row = row0 + (okt ? t : 0);
+            cp_async16(&st.dtq[r][4 * q], src.dtq + row * src.ldq + 16 * q, okt);
+        }
+        if (lane < 4) {
+            const int r = 4 * hf + lane;
+            const int t = t0 + r;
+            cp_async4(&st.dts[r], src.dts + row0 + (t < L ? t : 0), t < L);
+        }
+    }
+}
+
+template <int RW>
+__global__ void __launch_bounds__(128)
+ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc, int ldbc, const DtSource src,
                     const float* __restrict__ z, int ldz, const float* __restrict__ base, float* __restrict__ y,
                     float* __restrict__ amax, float* __restrict__ h_out, int L, int D) {
-    static_assert(WS3_LA <= WS3_NR - 3, "the ring holds a slot in each phase plus the staged ones");
-    static_assert(3 * WS3_NR + 1 <= 16, "named barrier ids");
-    __shared__ __align__(16) ScanStage ring[WS3_NR];
-    __shared__ unsigned fmask[WS3_NR];
+    __shared__ __align__(16) ScanStage ring[PIPE_NR];
+    __shared__ unsigned fmask2[PIPE_NR][2];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.y;
     const int d0 = blockIdx.x * 32;
@@ -607,9 +652,9 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
     const int dd = active ? d : 0;
     const size_t row0 = (size_t)b * L;
     const int nchunks = cdiv(L, SC);
-    constexpr int BA = 1, BB = 1 + WS3_NR, BG = 1 + 2 * WS3_NR;  // barrier id bases (0 is __syncthreads)
-    if (warp == 1) {
-        // ---- recurrence (same operations as ssm_scan_kernel<RW, 1>, phase B)
+    constexpr int BA = 1, BB = 1 + PIPE_NR, BG = 1 + 2 * PIPE_NR;  // barrier id bases (0 is __syncthreads)
+    if (warp == 2) {
+        // ---- recurrence and h.C (ssm_scan_kernel<RW, 1>, phase B)
         float h[NS], bsl[NS];
 #pragma unroll
         for (int n = 0; n < NS; n++) {
@@ -617,10 +662,10 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
             h[n] = 0.0f;
         }
         for (int c = 0; c < nchunks; c++) {
-            const int s = c % WS3_NR;
-            named_sync(BA + s, 64);
+            const int s = c % PIPE_NR;
+            named_sync(BA + s, 96);
             ScanStage& st = ring[s];
-            const unsigned fm = fmask[s];
+            const unsigned fm = fmask2[s][0] | fmask2[s][1];
             const int tn = min(SC, L - c * SC);
             if (tn == SC && fm == (1u << SC) - 1) {
 #pragma unroll
@@ -673,10 +718,10 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
         }
         return;
     }
-    if (warp == 2) {
-        // ---- gate, store, row absmax (phase C of ssm_scan_kernel)
+    if (warp == 3) {
+        // ---- gate, store, row absmax (ssm_scan_kernel<RW, 1>, phase C)
         for (int c = 0; c < nchunks; c++) {
-            const int s = c % WS3_NR;
+            const int s = c % PIPE_NR;
             named_sync(BB + s, 64);
             ScanStage& st = ring[s];
             const int t0 = c * SC;
@@ -689,7 +734,7 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
                 m[j] = (j < tn && active) ? __float_as_uint(fabsf(out)) : 0u;
             }
             __syncwarp();
-            if (c < nchunks - WS3_NR) named_arrive(BG + s, 64);  // the slot is restaged with chunk c + NR
+            if (c < nchunks - PIPE_NR) named_arrive(BG + s, 96);  // the slot is restaged with chunk c + NR
             if (amax) {
                 const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
                 unsigned m2[4], m3[2];
@@ -717,7 +762,8 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
         }
         return;
     }
-    // ---- staging and phase A (ssm_scan_kernel<RW, 1>, phase A)
+    // ---- warps 0 and 1: staging and phase A of steps 4*hf .. 4*hf+3 (ssm_scan_kernel<RW, 1>, phase A)
+    const int hf = warp;
     int32_t wd[RW > 0 ? RW : 1];
     float wsc = 0.0f;
     if (RW > 0) {
@@ -740,26 +786,28 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
     }
     const bool wide_ok = !bnan && (bmin >= 37.0f) && (bmax <= 63963.0f);  // see ssm_scan_kernel
 #pragma unroll
-    for (int c = 0; c < WS3_LA; c++) {
-        if (c < nchunks) scan_stage_load<RW, 32>(ring[c], act, src, z, bc, ldbc, ldz, row0, c * SC, L, d0, D);
+    for (int c = 0; c < PIPE_LA; c++) {
+        if (c < nchunks) stage_half<RW>(ring[c], act, src, z, bc, ldbc, ldz, row0, c * SC, L, d0, D, hf);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
     }
     for (int c = 0; c < nchunks; c++) {
-        const int cn = c + WS3_LA;
+        const int cn = c + PIPE_LA;
         if (cn < nchunks) {
-            const int sn = cn % WS3_NR;
-            if (cn >= WS3_NR) named_sync(BG + sn, 64);  // the gate warp is done with chunk cn - NR
-            scan_stage_load<RW, 32>(ring[sn], act, src, z, bc, ldbc, ldz, row0, cn * SC, L, d0, D);
+            const int sn = cn % PIPE_NR;
+            if (cn >= PIPE_NR) named_sync(BG + sn, 96);  // the gate warp is done with chunk cn - NR
+            stage_half<RW>(ring[sn], act, src, z, bc, ldbc, ldz, row0, cn * SC, L, d0, D, hf);
         }
         asm volatile("cp.async.commit_group;\n" ::: "memory");
-        asm volatile("cp.async.wait_group %0;\n" ::"n"(WS3_LA) : "memory");
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(PIPE_LA) : "memory");
         __syncwarp();
-        const int s = c % WS3_NR;
+        const int s = c % PIPE_NR;
         ScanStage& st = ring[s];
-        float modr[SC];
-        if (RW > 0) {
+        unsigned fast_mask = 0;
 #pragma unroll
-            for (int j = 0; j < SC; j++) {
+        for (int jj = 0; jj < 4; jj++) {
+            const int j = 4 * hf + jj;
+            float mr;
+            if (RW > 0) {
                 const int4* q4 = reinterpret_cast<const int4*>(&st.dtq[j][0]);
                 int acc0 = 0, acc1 = 0;  // exact: integer sums in any order
 #pragma unroll
@@ -770,16 +818,11 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
                     acc0 = __dp4a(qv.z, wd[4 * k + 2], acc0);
                     acc1 = __dp4a(qv.w, wd[4 * k + 3], acc1);
                 }
-                modr[j] = __fmul_rn((float)(acc0 + acc1), __fmul_rn(wsc, st.dts[j]));
+                mr = __fmul_rn((float)(acc0 + acc1), __fmul_rn(wsc, st.dts[j]));
+            } else {
+                mr = st.mod[j][lane];
             }
-        } else {
-#pragma unroll
-            for (int j = 0; j < SC; j++) modr[j] = st.mod[j][lane];
-        }
-        unsigned fast_mask = 0;
-#pragma unroll
-        for (int j = 0; j < SC; j++) {
-            const float mod = ste_clamp(modr[j], -20.0f, 20.0f);
+            const float mod = ste_clamp(mr, -20.0f, 20.0f);
             const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);
             bool inside = (mod == 0.0f || fabsf(mod) >= 1e-30f);
             if (!wide_ok)
@@ -789,9 +832,9 @@ ssm_scan_ws3_kernel(const float* __restrict__ act, const float* __restrict__ bc,
             st.mod[j][lane] = mod;
             st.act[j][lane] = __fmul_rn(st.act[j][lane], dtv);  // x * dt_val
         }
-        if (lane == 0) fmask[s] = fast_mask;
+        if (lane == 0) fmask2[s][hf] = fast_mask;
         __syncwarp();
-        named_arrive(BA + s, 64);
+        named_arrive(BA + s, 96);
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 }
@@ -1101,22 +1144,14 @@ extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, 
 namespace mi {
 namespace ssm {
 
-// Kernel choice: one lane per channel (ssm_scan_kernel) when the layer's
-// (sequence, 32-channel) groups give at least 8 warps per SM; below that the
-// three-warp pipeline (ssm_scan_ws3_kernel).  2, 4 or 8 lanes per channel
-// (ssm_scan_split_kernel) stay available by explicit request.
+// Kernel choice: the pipelined kernel (ssm_scan_pipe_kernel), measured
+// faster than one lane per channel (ssm_scan_kernel) and than 2, 4 or 8
+// lanes (ssm_scan_split_kernel) at per-GPU batches 8, 16, 32 and 64 of the
+// config-4 layer; the others stay available by explicit request.
 static int pick_split(int batch, int D) {
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
-    const long long want = 8LL * sms;
-    const long long units = (long long)batch * cdiv(D, 32);  // (sequence, 32-channel group) pairs
-    if (units >= want) return 1;
-    return 3;  // the three-warp pipeline (measured faster than 2 or 4 lanes per channel there)
+    (void)batch;
+    (void)D;
+    return 3;
 }
 
 template <int RW>
@@ -1125,7 +1160,7 @@ static void launch_scan(int split, int batch, int L, int D, const float* act, co
                         float* h_out, cudaStream_t s) {
     if (split == 3) {
         dim3 grid(cdiv(D, 32), batch);
-        ssm_scan_ws3_kernel<RW><<<grid, 96, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
+        ssm_scan_pipe_kernel<RW><<<grid, 128, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
         return;
     }
     const int chw = SCAN_THREADS / split;

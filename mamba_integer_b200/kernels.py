@@ -247,7 +247,7 @@ def ssm_scan_dt(act, bc, dtq, dts, w_dt, w_dt_scale, R: int, z, base, batch: int
                 split: int = 0, h_out=None):
     """ssm_scan with dt_proj fused (see mi_ssm_scan_dt): dtq int8 [T, ldq] quantised
     dt rows, dts [T] their scales, w_dt int8 [D, ceil16(R)], w_dt_scale [1].
-    split: kernel variant (1/2/4/8 lanes per channel, 3 = three-warp pipeline,
+    split: kernel variant (1/2/4/8 lanes per channel, 3 = pipelined (four warps),
     0 = automatic); h_out [batch, D, N]: final states."""
     D, N = base.shape
     T = batch * L
