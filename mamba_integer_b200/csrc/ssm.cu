@@ -584,17 +584,30 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
 // restaged), and a warp reaches a slot's barrier for chunk c + NR only after
 // the other warps have passed it for chunk c.  The arithmetic is that of
 // ssm_scan_kernel<RW, 1>.
-constexpr int PIPE_NR = 5;  // ring slots
-constexpr int PIPE_LA = 2;  // chunks staged ahead of the one in phase A
+constexpr int PIPE_NR = 4;  // ring slots (3 barriers each: 12 ids keep 5 CTAs per SM possible)
+constexpr int PIPE_LA = 1;  // chunks staged ahead of the one in phase A
 static_assert(PIPE_LA <= PIPE_NR - 3, "the ring holds a slot in each phase plus the staged ones");
-static_assert(3 * PIPE_NR + 1 <= 16, "named barrier ids");
+static_assert(3 * PIPE_NR <= 16, "named barrier ids");
 
-__device__ __forceinline__ void named_arrive(int id, int n) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
-__device__ __forceinline__ void named_sync(int id, int n) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
+// Named barrier `id` in [I, N) issued with its id as an immediate (a run-time
+// id makes the compiler reserve all 16 hardware barriers of the CTA, which
+// caps the CTAs per SM; immediates reserve only ids below N).
+template <int I, int N>
+struct NamedBar {
+    __device__ __forceinline__ static void arrive(int id, int n) {
+        if (id == I) asm volatile("bar.arrive %0, %1;" ::"n"(I), "r"(n) : "memory");
+        else NamedBar<I + 1, N>::arrive(id, n);
+    }
+    __device__ __forceinline__ static void sync(int id, int n) {
+        if (id == I) asm volatile("bar.sync %0, %1;" ::"n"(I), "r"(n) : "memory");
+        else NamedBar<I + 1, N>::sync(id, n);
+    }
+};
+template <int N>
+struct NamedBar<N, N> {
+    __device__ __forceinline__ static void arrive(int, int) {}
+    __device__ __forceinline__ static void sync(int, int) {}
+};
 
 // Stage rows 4*hf .. 4*hf+3 of chunk [t0, t0+SC) (32 channels) into `st`.
 template <int RW>
@@ -652,7 +665,8 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
     const int dd = active ? d : 0;
     const size_t row0 = (size_t)b * L;
     const int nchunks = cdiv(L, SC);
-    constexpr int BA = 1, BB = 1 + PIPE_NR, BG = 1 + 2 * PIPE_NR;  // barrier id bases (0 is __syncthreads)
+    constexpr int BA = 0, BB = PIPE_NR, BG = 2 * PIPE_NR;  // barrier id bases (no __syncthreads here)
+    using Bar = NamedBar<0, 3 * PIPE_NR>;
     if (warp == 2) {
         // ---- recurrence and h.C (ssm_scan_kernel<RW, 1>, phase B)
         float h[NS], bsl[NS];
@@ -663,7 +677,7 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
         }
         for (int c = 0; c < nchunks; c++) {
             const int s = c % PIPE_NR;
-            named_sync(BA + s, 96);
+            Bar::sync(BA + s, 96);
             ScanStage& st = ring[s];
             const unsigned fm = fmask2[s][0] | fmask2[s][1];
             const int tn = min(SC, L - c * SC);
@@ -709,7 +723,7 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
                 }
             }
             __syncwarp();
-            named_arrive(BB + s, 64);
+            Bar::arrive(BB + s, 64);
         }
         if (h_out && active) {
             float* dst = h_out + ((size_t)b * D + d) * NS;
@@ -722,7 +736,7 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
         // ---- gate, store, row absmax (ssm_scan_kernel<RW, 1>, phase C)
         for (int c = 0; c < nchunks; c++) {
             const int s = c % PIPE_NR;
-            named_sync(BB + s, 64);
+            Bar::sync(BB + s, 64);
             ScanStage& st = ring[s];
             const int t0 = c * SC;
             const int tn = min(SC, L - t0);
@@ -734,7 +748,7 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
                 m[j] = (j < tn && active) ? __float_as_uint(fabsf(out)) : 0u;
             }
             __syncwarp();
-            if (c < nchunks - PIPE_NR) named_arrive(BG + s, 96);  // the slot is restaged with chunk c + NR
+            if (c < nchunks - PIPE_NR) Bar::arrive(BG + s, 96);  // the slot is restaged with chunk c + NR
             if (amax) {
                 const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4;
                 unsigned m2[4], m3[2];
@@ -794,7 +808,7 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
         const int cn = c + PIPE_LA;
         if (cn < nchunks) {
             const int sn = cn % PIPE_NR;
-            if (cn >= PIPE_NR) named_sync(BG + sn, 96);  // the gate warp is done with chunk cn - NR
+            if (cn >= PIPE_NR) Bar::sync(BG + sn, 96);  // the gate warp is done with chunk cn - NR
             stage_half<RW>(ring[sn], act, src, z, bc, ldbc, ldz, row0, cn * SC, L, d0, D, hf);
         }
         asm volatile("cp.async.commit_group;\n" ::: "memory");
@@ -834,7 +848,7 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
         }
         if (lane == 0) fmask2[s][hf] = fast_mask;
         __syncwarp();
-        named_arrive(BA + s, 96);
+        Bar::arrive(BA + s, 96);
     }
     asm volatile("cp.async.wait_group 0;\n" ::: "memory");
 }
@@ -1159,6 +1173,12 @@ static void launch_scan(int split, int batch, int L, int D, const float* act, co
                         const DtSource& src, const float* z, int ldz, const float* base, float* y, float* amax,
                         float* h_out, cudaStream_t s) {
     if (split == 3) {
+        static bool carveout_set = false;
+        if (!carveout_set) {  // 20 KB of shared memory per CTA: let registers bound the residency
+            cudaFuncSetAttribute(ssm_scan_pipe_kernel<RW>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                 cudaSharedmemCarveoutMaxShared);
+            carveout_set = true;
+        }
         dim3 grid(cdiv(D, 32), batch);
         ssm_scan_pipe_kernel<RW><<<grid, 128, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
         return;
