@@ -366,28 +366,65 @@ __device__ __forceinline__ bool argmax_better(float v, int i, float bv, int bi) 
     return v > bv || (v == bv && i < bi);
 }
 
-__global__ void __launch_bounds__(STEP_THREADS)
+__device__ __forceinline__ void argmax_take(float v, int i, float& bv, int& bi) {
+    if (argmax_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+// One CTA of ARGMAX_THREADS per row.  (value, index) pairs are compared by a
+// total order, so partial results merge in any order: each thread keeps four
+// running maxima (one per float4 component) over 16-byte loads, two loads in
+// flight, and the block merges them; rows that are not 16-byte aligned or
+// whose width is not a multiple of 4 are scanned element by element.
+constexpr int ARGMAX_THREADS = 512;
+__global__ void __launch_bounds__(ARGMAX_THREADS)
 argmax_rows_kernel(const float* __restrict__ x, int ldx, int V, int64_t* __restrict__ out) {
-    __shared__ float sv[STEP_THREADS / 32];
-    __shared__ int si[STEP_THREADS / 32];
+    __shared__ float sv[ARGMAX_THREADS / 32];
+    __shared__ int si[ARGMAX_THREADS / 32];
     const float* row = x + (size_t)blockIdx.x * ldx;
-    float bv = -__int_as_float(0x7f800000);
+    const float ninf = -__int_as_float(0x7f800000);
+    float bv = ninf;
     int bi = 0x7fffffff;
-    for (int k = threadIdx.x; k < V; k += STEP_THREADS) {
-        const float v = row[k];
-        if (argmax_better(v, k, bv, bi)) {
-            bv = v;
-            bi = k;
+    if (((uintptr_t)row & 15) == 0 && (V & 3) == 0) {
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+        const int V4 = V >> 2;
+        float v0 = ninf, v1 = ninf, v2 = ninf, v3 = ninf;
+        int i0 = 0x7fffffff, i1 = 0x7fffffff, i2 = 0x7fffffff, i3 = 0x7fffffff;
+        int k = threadIdx.x;
+        for (; k + ARGMAX_THREADS < V4; k += 2 * ARGMAX_THREADS) {
+            const float4 a = row4[k], c = row4[k + ARGMAX_THREADS];
+            argmax_take(a.x, 4 * k, v0, i0);
+            argmax_take(a.y, 4 * k + 1, v1, i1);
+            argmax_take(a.z, 4 * k + 2, v2, i2);
+            argmax_take(a.w, 4 * k + 3, v3, i3);
+            const int kc = 4 * (k + ARGMAX_THREADS);
+            argmax_take(c.x, kc, v0, i0);
+            argmax_take(c.y, kc + 1, v1, i1);
+            argmax_take(c.z, kc + 2, v2, i2);
+            argmax_take(c.w, kc + 3, v3, i3);
         }
+        if (k < V4) {
+            const float4 a = row4[k];
+            argmax_take(a.x, 4 * k, v0, i0);
+            argmax_take(a.y, 4 * k + 1, v1, i1);
+            argmax_take(a.z, 4 * k + 2, v2, i2);
+            argmax_take(a.w, 4 * k + 3, v3, i3);
+        }
+        bv = v0;
+        bi = i0;
+        argmax_take(v1, i1, bv, bi);
+        argmax_take(v2, i2, bv, bi);
+        argmax_take(v3, i3, bv, bi);
+    } else {
+        for (int k = threadIdx.x; k < V; k += ARGMAX_THREADS) argmax_take(row[k], k, bv, bi);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (argmax_better(ov, oi, bv, bi)) {
-            bv = ov;
-            bi = oi;
-        }
+        argmax_take(ov, oi, bv, bi);
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
@@ -396,16 +433,13 @@ argmax_rows_kernel(const float* __restrict__ x, int ldx, int V, int64_t* __restr
     }
     __syncthreads();
     if (warp == 0) {
-        bv = lane < STEP_THREADS / 32 ? sv[lane] : -__int_as_float(0x7f800000);
-        bi = lane < STEP_THREADS / 32 ? si[lane] : 0x7fffffff;
+        bv = lane < ARGMAX_THREADS / 32 ? sv[lane] : ninf;
+        bi = lane < ARGMAX_THREADS / 32 ? si[lane] : 0x7fffffff;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
             const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (argmax_better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
-            }
+            argmax_take(ov, oi, bv, bi);
         }
         // a row of -inf only: every element ties, index 0
         if (lane == 0) out[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
@@ -468,7 +502,7 @@ extern "C" int mi_decode_mid(const float* xz, int ldx, const float* conv_w, cons
 extern "C" int mi_argmax_rows(const float* x, int ldx, int T, int V, int64_t* out, void* stream) {
     using namespace mi::decode;
     if (!x || !out || T <= 0 || V <= 0 || ldx < V) return MI_ERR_INVALID;
-    argmax_rows_kernel<<<T, STEP_THREADS, 0, (cudaStream_t)stream>>>(x, ldx, V, out);
+    argmax_rows_kernel<<<T, ARGMAX_THREADS, 0, (cudaStream_t)stream>>>(x, ldx, V, out);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

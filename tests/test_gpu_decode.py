@@ -99,6 +99,28 @@ def test_prefill_final_states_match_oracle(cuda_dev):
         assert np.array_equal(h.cpu().numpy().view(np.uint32), h_ref.view(np.uint32)), split
 
 
+@pytest.mark.parametrize("V,ld", [(32768, 32768), (1001, 1001), (4096, 4100), (6, 6)])
+def test_argmax_rows_matches_torch(cuda_dev, V, ld):
+    """Full-vocabulary rows (16-byte loads), widths that are not a multiple of 4
+    and strided rows (element by element); ties and NaNs placed on different
+    float4 components and threads."""
+    from mamba_integer_b200 import kernels
+    g = torch.Generator().manual_seed(V + ld)
+    full = torch.randn(9, ld, generator=g)
+    x = full[:, :V]
+    x[0, V - 1] = x[0, 1] = 9.0         # tie: the lower index, other component
+    x[1, min(V - 1, V // 2 + 2)] = x[1, min(V - 1, V // 2 + 2) - 1] = 9.0
+    x[2, V - 2] = float("nan")
+    x[2, V // 3] = float("nan")         # first NaN wins
+    x[3, :] = -float("inf")
+    x[4, :] = 1.0                       # all equal: index 0
+    x[5, V - 1] = float("inf")
+    x[6, min(5, V - 1)] = 7.0
+    x[6, V - 1] = 7.0
+    got = kernels.argmax_rows(x.to(cuda_dev)).cpu()
+    assert got.tolist() == torch.argmax(x, dim=-1).tolist()
+
+
 def test_argmax_rows_ties_nan_and_inf(cuda_dev):
     from mamba_integer_b200 import kernels
     x = torch.randn(6, 1000)
