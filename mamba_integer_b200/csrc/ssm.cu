@@ -104,16 +104,28 @@ conv_act_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__
 // pass over act, no atomics, no workspace.  Same arithmetic as
 // conv_act_kernel followed by quant_rows_kernel.
 constexpr int CONVR_G = 4;  // positions per group (one block reduction each group)
+constexpr int CONVR_RING = 3;  // groups of input rows staged in shared memory
+
+__device__ __forceinline__ void conv_cp16(float* smem, const float* gmem, bool pred) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(gmem), "r"(pred ? 16 : 0)
+                 : "memory");
+}
 
 // MAXT = the CTA size it is compiled for: up to 384 threads (D <= 1536) it
 // gets up to 80 registers at two CTAs per SM and computes the channels in
 // f32x2 pairs; up to 1024 threads it stays within 64 registers, scalar.
+// The input rows arrive through a ring of CONVR_RING groups in dynamic shared
+// memory ([CONVR_RING][CONVR_G][D] floats), two groups ahead of the one being
+// computed; each thread copies and reads only its own 16-byte chunks, so the
+// ring needs no barrier of its own.
 template <int MAXT>
 __global__ void __launch_bounds__(MAXT, MAXT <= 384 ? 2 : 1)
 conv_rows_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ w, const float* __restrict__ bias,
                  float* __restrict__ act, int8_t* __restrict__ xq, float* __restrict__ xscale, int L, int D) {
     constexpr bool PAIRED = MAXT <= 384;
     __shared__ unsigned red[2][CONVR_G][32];  // per position: each warp's max |act| bits (double buffer)
+    extern __shared__ __align__(16) float xring[];
     const int c = 4 * threadIdx.x;  // first of this thread's 4 channels
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int b = blockIdx.y;
@@ -131,12 +143,28 @@ conv_rows_kernel(const float* __restrict__ xz, int ldx, const float* __restrict_
     float4 w1 = (t0 - 2 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 2) * ldx) : zero4;
     float4 w2 = (t0 - 1 >= 0) ? *reinterpret_cast<const float4*>(px + (size_t)(t0 - 1) * ldx) : zero4;
     const int tend = min(L, t0 + CONV_TC);
-    int buf = 0;
-    for (int t = t0; t < tend; t += CONVR_G, buf ^= 1) {
+    // rows t .. t + CONVR_G - 1 into ring slot `slot` (rows past tend read as zero)
+    auto stage = [&](int t, int slot) {
+        if (active) {
+#pragma unroll
+            for (int j = 0; j < CONVR_G; j++) {
+                const bool ok = t + j < tend;
+                conv_cp16(xring + (size_t)(slot * CONVR_G + j) * D + c, px + (size_t)(ok ? t + j : t0) * ldx, ok);
+            }
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    stage(t0, 0);
+    stage(t0 + CONVR_G, 1);
+    int buf = 0, slot = 0;
+    for (int t = t0; t < tend; t += CONVR_G, buf ^= 1, slot = slot == CONVR_RING - 1 ? 0 : slot + 1) {
         float4 a[CONVR_G];
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // this group's rows have landed
 #pragma unroll
         for (int j = 0; j < CONVR_G; j++)
-            a[j] = (t + j < tend) ? __ldg(reinterpret_cast<const float4*>(px + (size_t)(t + j) * ldx)) : zero4;
+            a[j] = active ? *reinterpret_cast<const float4*>(xring + (size_t)(slot * CONVR_G + j) * D + c) : zero4;
+        // the group after next goes to the slot read two groups ago
+        stage(t + 2 * CONVR_G, slot == 0 ? CONVR_RING - 1 : slot - 1);
         unsigned m[CONVR_G];
 #pragma unroll
         for (int j = 0; j < CONVR_G; j++) {
@@ -1145,12 +1173,21 @@ extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, 
     if (batch > 65535) return MI_ERR_UNSUPPORTED;
     const int threads = mi::cdiv(D / 4, 32) * 32;
     dim3 grid(mi::cdiv(L, mi::ssm::CONV_TC), batch);
+    const size_t ring = (size_t)mi::ssm::CONVR_RING * mi::ssm::CONVR_G * D * sizeof(float);
+    static bool attr_set = false;
+    if (!attr_set) {  // the ring: up to 72 KB (D <= 1536) / 192 KB (D <= 4096) of dynamic shared memory
+        cudaFuncSetAttribute(mi::ssm::conv_rows_kernel<384>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mi::ssm::CONVR_RING * mi::ssm::CONVR_G * 1536 * (int)sizeof(float));
+        cudaFuncSetAttribute(mi::ssm::conv_rows_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mi::ssm::CONVR_RING * mi::ssm::CONVR_G * 4096 * (int)sizeof(float));
+        attr_set = true;
+    }
     if (threads <= 384)
-        mi::ssm::conv_rows_kernel<384><<<grid, threads, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale, L,
-                                                                                  D);
+        mi::ssm::conv_rows_kernel<384><<<grid, threads, ring, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale,
+                                                                                     L, D);
     else
-        mi::ssm::conv_rows_kernel<1024><<<grid, threads, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale,
-                                                                                   L, D);
+        mi::ssm::conv_rows_kernel<1024><<<grid, threads, ring, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq,
+                                                                                      xscale, L, D);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
