@@ -104,6 +104,11 @@ __device__ __forceinline__ float squareplus(float x) {
 // differs from c by at most half an ulp of x, and when that exceeds the bound
 // the difference c - x rounds to -x and the result is 0, so the magnitude
 // never exceeds 2 * 50.
+// The upper clamp of each Newton step (r <= 1e3) is skipped too: y > 0 and
+// r > 0 make t = (0.5*y*r)*r >= 0, so 1.5 - t <= 1.5 and each step at most
+// multiplies r by fl(1.5); from a guess <= 0.5, r stays below 1.7 after three
+// steps.  A NaN or +inf y gives the same r with or without it (NaN, and the
+// lower clamp 1e-6, respectively).
 __device__ __forceinline__ float squareplus_bounded(float x) {
     const float y = __fadd_rn(__fmul_rn(x, x), 4.0f);
     float r = (y > 16.0f) ? 0.125f : 0.5f;
@@ -116,7 +121,7 @@ __device__ __forceinline__ float squareplus_bounded(float x) {
         t = __fmul_rn(t, r);
         t = __fsub_rn(1.5f, t);
         r = __fmul_rn(r, t);
-        r = clamp_t(r, 1e-6f, 1e3f);
+        r = max_nan(r, 1e-6f);  // the upper clamp never binds here (see above)
     }
     const float s = clamp_t(__fmul_rn(y, r), 0.0f, 1e3f);
     return __fmul_rn(0.5f, __fadd_rn(x, s));
@@ -155,7 +160,7 @@ __device__ __forceinline__ float2 squareplus_bounded2(float2 x) {
         t = __fmul2_rn(t, r);
         t = make_float2(__fsub_rn(1.5f, t.x), __fsub_rn(1.5f, t.y));
         r = __fmul2_rn(r, t);
-        r = make_float2(clamp_t(r.x, 1e-6f, 1e3f), clamp_t(r.y, 1e-6f, 1e3f));
+        r = make_float2(max_nan(r.x, 1e-6f), max_nan(r.y, 1e-6f));  // as in squareplus_bounded
     }
     const float2 p = __fmul2_rn(y, r);
     const float2 sq = make_float2(clamp_t(p.x, 0.0f, 1e3f), clamp_t(p.y, 0.0f, 1e3f));
