@@ -1174,13 +1174,13 @@ extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, 
     const int threads = mi::cdiv(D / 4, 32) * 32;
     dim3 grid(mi::cdiv(L, mi::ssm::CONV_TC), batch);
     const size_t ring = (size_t)mi::ssm::CONVR_RING * mi::ssm::CONVR_G * D * sizeof(float);
-    static bool attr_set = false;
-    if (!attr_set) {  // the ring: up to 72 KB (D <= 1536) / 192 KB (D <= 4096) of dynamic shared memory
-        cudaFuncSetAttribute(mi::ssm::conv_rows_kernel<384>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             mi::ssm::CONVR_RING * mi::ssm::CONVR_G * 1536 * (int)sizeof(float));
-        cudaFuncSetAttribute(mi::ssm::conv_rows_kernel<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             mi::ssm::CONVR_RING * mi::ssm::CONVR_G * 4096 * (int)sizeof(float));
-        attr_set = true;
+    // the ring: up to 72 KB (D <= 1536) / 192 KB (D <= 4096) of dynamic shared memory; the
+    // attribute belongs to the current device's context, so it is set on every call
+    if (cudaFuncSetAttribute(threads <= 384 ? (const void*)mi::ssm::conv_rows_kernel<384>
+                                            : (const void*)mi::ssm::conv_rows_kernel<1024>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ring) != cudaSuccess) {
+        cudaGetLastError();  // reported here; keep it out of later launch checks
+        return MI_ERR_CUDA;
     }
     if (threads <= 384)
         mi::ssm::conv_rows_kernel<384><<<grid, threads, ring, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale,
@@ -1210,12 +1210,10 @@ static void launch_scan(int split, int batch, int L, int D, const float* act, co
                         const DtSource& src, const float* z, int ldz, const float* base, float* y, float* amax,
                         float* h_out, cudaStream_t s) {
     if (split == 3) {
-        static bool carveout_set = false;
-        if (!carveout_set) {  // 20 KB of shared memory per CTA: let registers bound the residency
-            cudaFuncSetAttribute(ssm_scan_pipe_kernel<RW>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                 cudaSharedmemCarveoutMaxShared);
-            carveout_set = true;
-        }
+        // 20 KB of shared memory per CTA: prefer the largest carveout so that registers bound
+        // the residency (a per-context preference, set on every call like the others)
+        cudaFuncSetAttribute(ssm_scan_pipe_kernel<RW>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
         dim3 grid(cdiv(D, 32), batch);
         ssm_scan_pipe_kernel<RW><<<grid, 128, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
         return;
