@@ -205,8 +205,9 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * acc * (w_dt_scale * dts[t]) itself.  R <= 64.
  * split = kernel variant: 1, 2, 4 or 8 lanes per channel, or 3 = one lane per
  * channel with each chunk's phases pipelined over four warps (two staging
- * and decay, recurrence, gate); 0 = automatic (currently 3, the fastest at
- * every measured batch).  All variants give identical results.
+ * and decay, recurrence, gate); 0 = automatic (3 from 64 positions on, where
+ * it measured fastest at every batch; 1 for shorter sequences).  All variants
+ * give identical results.
  * h_out (optional, [batch, D, N], 16-byte aligned) receives the states after
  * the last position (the starting point of mi_ssm_step).
  * Replaces: dt_proj + DyadicScanFunction section, src/mamba_integer_model.py:419-444
