@@ -182,6 +182,45 @@ quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __
     }
 }
 
+// quant_rows_kernel for rows of at most 64 values without a given absmax (the
+// dt rows of the fused scan): half a warp per row, up to 4 values per lane,
+// two rows per warp at once -- the same operations per element, the row's
+// absmax and NaN flag reduced over its 16 lanes.
+__global__ void __launch_bounds__(256)
+quant_rows_narrow_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __restrict__ xq, int ldq,
+                         float* __restrict__ xscale) {
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
+    const int rows_per_cta = (blockDim.x >> 5) * 2;
+    for (int t0 = blockIdx.x * rows_per_cta; t0 < T; t0 += gridDim.x * rows_per_cta) {
+        const int t = t0 + (threadIdx.x >> 5) * 2 + half;
+        const bool okr = t < T;
+        float v[4];
+        float am = 0.0f;
+        bool nan = false;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int k = 4 * hl + e;
+            v[e] = (okr && k < K) ? x[(size_t)t * ldx + k] : 0.0f;
+            const float a = fabsf(v[e]);
+            nan |= (a != a);
+            am = fmaxf(am, a);
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(FULL, am, o));
+        const bool rnan = (__ballot_sync(FULL, nan) >> (16 * half)) & 0xffffu;
+        const float amax = rnan ? __int_as_float(0x7fc00000) : am;
+        const float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
+        const float inv = __fmul_rn(__frcp_rn(sc), 127.0f);
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int k = 4 * hl + e;
+            if (okr && k < K) xq[(size_t)t * ldq + k] = (int8_t)quant_i8(__fmul_rn(v[e], inv));
+        }
+        if (okr && hl == 0) xscale[t] = __fdiv_rn(sc, 127.0f);
+    }
+}
+
 typedef void (*rowprep_fn)(const float*, const float*, const float*, const int64_t*, const float*, int, float*,
                            const float*, const float*, float*, int8_t*, float*, float*, int, int);
 
@@ -258,6 +297,14 @@ extern "C" int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* x
     if (T < 0 || K <= 0 || ldx < K || ldq < K) return MI_ERR_INVALID;
     if (T == 0) return MI_OK;
     const int threads = 256;
+    if (!amax && K <= 64) {  // narrow rows: two per warp
+        int blocks = mi::cdiv(T, threads / 16);
+        if (blocks > 148 * 16) blocks = 148 * 16;
+        mi::rowops::quant_rows_narrow_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq,
+                                                                                           xscale);
+        MI_CHECK_LAUNCH();
+        return MI_OK;
+    }
     int blocks = mi::cdiv(T, threads / 32);
     if (blocks > 148 * 16) blocks = 148 * 16;
     mi::rowops::quant_rows_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq, xscale, amax);

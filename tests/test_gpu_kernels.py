@@ -185,6 +185,30 @@ def test_quantize_rows_matches_oracle(cuda_dev, K):
     _eq(s, s_ref, "xscale")
 
 
+@pytest.mark.parametrize("K", [1, 7, 33, 64])
+def test_quantize_rows_narrow_strided(cuda_dev, K):
+    """Rows of at most 64 values (two per warp) read from a wider strided
+    array: ragged widths, a NaN row, zero and infinite rows, row counts that
+    leave a warp half empty."""
+    k = _mi()
+    g = np.random.default_rng(K)
+    T = 301
+    wide = (g.standard_normal((T, K + 5)) * np.logspace(-3, 3, T)[:, None]).astype(np.float32)
+    wide[3, :K] = 0.0
+    wide[4, K // 2] = np.nan
+    wide[5, 0] = np.inf
+    wide[6, :K] = 127.0 / 3
+    x = np.ascontiguousarray(wide[:, :K])
+    q_ref, s_ref = orc.quant_rows(x)
+    xd = torch.from_numpy(wide).to(cuda_dev)[:, :K]
+    q, s = k.quantize_rows(xd)
+    _eq(q, q_ref, "xq")
+    # the NaN row's scale is NaN on both sides; its payload bits are not specified
+    s = s.cpu().numpy()
+    assert np.array_equal(np.isnan(s), np.isnan(s_ref))
+    _eq(s[~np.isnan(s)], s_ref[~np.isnan(s_ref)], "xscale")
+
+
 @pytest.mark.parametrize("D", [256, 768])
 def test_rowprep_fused_matches_oracle(cuda_dev, D):
     k = _mi()
