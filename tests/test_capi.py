@@ -47,5 +47,14 @@ def test_host_side_argument_errors_need_no_gpu(lib):
     assert lib.mi_bitlinear_i8(None, 16, None, None, None, None, None, 16, 16, 16, 16, 0, None) == -1
     assert lib.mi_bitlinear_packed(None, 16, None, None, None, None, None, 16, 16, 16, 64, 0, None) == -1
     assert lib.mi_pack_ternary(None, 16, None, 1, 16, None) == -1
+    # the fused scan's kernel variant: 0 (automatic), 1, 2, 3, 4, 8 only (dummy aligned
+    # pointers: the call returns before it touches them)
+    p = 256
+    for split in (5, 6, 7, -1, 16):
+        assert lib.mi_ssm_scan_dt(p, p, 32, p, 48, p, p, p, 48, p, 64, p, p, None, None, 1, 8, 64, 16, split,
+                                  None) == -1, split
+    assert lib.mi_argmax_rows(None, 16, 1, 16, None, None) == -1
+    # row conv: at most 4096 channels
+    assert lib.mi_conv_act_quant_rows(p, 8200, p, p, p, p, p, 1, 8, 4100, None) == -2
     assert lib.mi_version() >= 1
     assert lib.mi_status_string(-2) == b"unsupported shape or configuration"
