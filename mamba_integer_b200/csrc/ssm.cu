@@ -614,7 +614,11 @@ ssm_scan_kernel(const float* __restrict__ act, const float* __restrict__ bc, int
 // ssm_scan_kernel<RW, 1>.
 constexpr int PIPE_NR = 4;  // ring slots (3 barriers each: 12 ids keep 5 CTAs per SM possible)
 constexpr int PIPE_LA = 1;  // chunks staged ahead of the one in phase A
-static_assert(PIPE_LA <= PIPE_NR - 3, "the ring holds a slot in each phase plus the staged ones");
+// Sizing, not safety: the gate-done barrier alone keeps restaging safe at any
+// staging distance (tests/test_pipe_protocol.py models the hand-offs); with
+// PIPE_LA <= PIPE_NR - 3 the staging warps need not wait for a chunk the gate
+// warp is still working on.
+static_assert(PIPE_LA <= PIPE_NR - 3, "ring sized for a slot in each phase plus the staged ones");
 static_assert(3 * PIPE_NR <= 16, "named barrier ids");
 
 // Named barrier `id` in [I, N) issued with its id as an immediate (a run-time
