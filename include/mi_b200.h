@@ -76,11 +76,13 @@ int mi_bitshift_norm(const float* x, const float* gamma, const float* step, floa
  *   xscale = s / 127.
  * x [T, >=K] row stride ldx; xq [T, >=K] row stride ldq (int8).
  * amax (optional, [T]): max|x| of each row already computed by the producer
- * of x (NULL: computed here).
+ * of x (NULL: computed here); it is consumed: each entry is read and then
+ * reset to 0, so a producer that accumulates row maxima by atomicMax (the
+ * fused scan) can reuse the array on the next call without a separate fill.
  * Replaces: fast_quantize_activations, src/triton_kernels/bitnet_kernels.py:98.
  */
 int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
-                     const float* amax, void* stream);
+                     float* amax, void* stream);
 
 /*
  * Row pre-pass in front of a BitLinear: optional residual update, BitShiftNorm,
@@ -171,9 +173,11 @@ int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, const float
  * cannot call cudaMalloc (a runtime whose device memory belongs to another
  * allocator, a serving loop that must not allocate).  No counterpart in the
  * reference.  The row-absmax scratch is a fixed array inside the library:
- * batch * L <= 262144 rows, larger requests return MI_ERR_UNSUPPORTED.  The
- * first call on a device looks the array's device address up (make that first
- * call before any stream capture).  Every call shares the array: calls that
+ * batch * L <= 262144 rows, larger requests return MI_ERR_UNSUPPORTED.  xq and
+ * xscale are required (this variant always quantises).  The first call on a
+ * device looks the array's device address up and keeps it for the life of the
+ * process (make that first call before any stream capture; do not call it on a
+ * device after cudaDeviceReset there).  Every call shares the array: calls that
  * overlap on the GPU race with each other; each call zero-fills the rows it
  * uses before using them.  Allocates nothing.
  */
@@ -186,9 +190,11 @@ int mi_conv_act_quant_noalloc(const float* xz, int ldx, const float* w, const fl
  * d = n/2^15, y = sum_n h*C (FMA, n ascending), gate y*sigmoid_alg(z).
  * act [batch*L, D]; bc rows (stride ldbc): B at [0,N), C at [N,2N);
  * modraw [batch*L, D]; z rows stride ldz; base [D,N]; y [batch*L, D].
- * amax (optional, [batch*L], zero-filled by the caller) receives max|y| per row
- * (feed it to mi_quantize_rows).
- * N == 16.
+ * amax (optional, [batch*L], zero on entry) receives max|y| per row (feed it
+ * to mi_quantize_rows, which resets it to zero).
+ * N == 16.  Results are the reference's bits; the one exception is the sign
+ * of a zero: where B holds -0.0 (the model's x_proj output never does), a
+ * state the reference leaves at -0.0 may come out +0.0.
  * Replaces: DyadicScanFunction.apply / dyadic_scan_triton_fast
  * (src/mamba_integer_model.py:419-444, src/triton_kernels/dyadic_scan.py:462).
  */
@@ -209,7 +215,8 @@ int mi_ssm_scan(const float* act, const float* bc, int ldbc, const float* modraw
  * it measured fastest at every batch; 1 for shorter sequences).  All variants
  * give identical results.
  * h_out (optional, [batch, D, N], 16-byte aligned) receives the states after
- * the last position (the starting point of mi_ssm_step).
+ * the last position (the starting point of mi_ssm_step).  The sign-of-zero
+ * note of mi_ssm_scan applies.
  * Replaces: dt_proj + DyadicScanFunction section, src/mamba_integer_model.py:419-444
  * (BitLinear rescale: src/rational_bitnet.py:204-208).
  */

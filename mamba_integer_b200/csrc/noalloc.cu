@@ -13,7 +13,10 @@
 // floats (1 MiB), which every GPU that loads the library keeps until the
 // process exits.  Host code cannot use the array's name as a device address,
 // so the first call on each device looks the address up with
-// cudaGetSymbolAddress (with that device current) and caches it.
+// cudaGetSymbolAddress (with that device current) and caches it for the life
+// of the process.  cudaDeviceReset destroys the context the array lives in and
+// the cached address with it: a process that resets a device must not call
+// this entry point on that device afterwards.
 #include <mutex>
 
 #include "mi_common.cuh"
@@ -30,14 +33,23 @@ static std::mutex g_lock;
 static float* g_scratch_ptr[MAX_DEVICES];  // device address of the array, per device
 
 // Device address of the scratch array on the current device (set-up on first use).
+// A failed runtime call is reported by this call only: its error is cleared from
+// the runtime's last-error state so that later, unrelated entry points (which
+// check cudaGetLastError after their launches) do not report it again.
 static int scratch_ptr(float** out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return MI_ERR_CUDA;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return MI_ERR_CUDA;
+    }
     if (dev < 0 || dev >= MAX_DEVICES) return MI_ERR_UNSUPPORTED;
     std::lock_guard<std::mutex> guard(g_lock);
     if (!g_scratch_ptr[dev]) {
         void* p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_conv_amax_scratch) != cudaSuccess || p == nullptr) return MI_ERR_CUDA;
+        if (cudaGetSymbolAddress(&p, g_conv_amax_scratch) != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return MI_ERR_CUDA;
+        }
         g_scratch_ptr[dev] = static_cast<float*>(p);
     }
     *out = g_scratch_ptr[dev];

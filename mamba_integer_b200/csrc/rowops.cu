@@ -157,7 +157,7 @@ rowprep_kernel(const float* x, const float* delta, const float* __restrict__ res
 // absmax, then quantise; the second pass re-reads the row from L1/L2).
 __global__ void __launch_bounds__(256)
 quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __restrict__ xq, int ldq,
-                  float* __restrict__ xscale, const float* __restrict__ amax_in) {
+                  float* __restrict__ xscale, float* __restrict__ amax_in) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
@@ -178,6 +178,12 @@ quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __
         float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
         float inv = __fmul_rn(__frcp_rn(sc), 127.0f);
         for (int k = lane; k < K; k += 32) xq[(size_t)t * ldq + k] = (int8_t)quant_i8(__fmul_rn(row[k], inv));
+        if (amax_in) {
+            // every lane has read the row's maximum: reset it to zero, so that a producer
+            // accumulating it by atomicMax can reuse the array without a fill
+            __syncwarp();
+            if (lane == 0) amax_in[t] = 0.0f;
+        }
         if (lane == 0) xscale[t] = __fdiv_rn(sc, 127.0f);
     }
 }
@@ -292,7 +298,7 @@ extern "C" int mi_rowprep(const float* x, const float* delta, const float* res_g
 }
 
 extern "C" int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
-                                const float* amax, void* stream) {
+                                float* amax, void* stream) {
     if (!x || !xq || !xscale) return MI_ERR_INVALID;
     if (T < 0 || K <= 0 || ldx < K || ldq < K) return MI_ERR_INVALID;
     if (T == 0) return MI_OK;

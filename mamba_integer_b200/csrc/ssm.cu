@@ -271,10 +271,19 @@ __device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool pre
 // Fast-path update of two states (see the decay comment in ssm_scan_kernel):
 //   dec = min(base/2^15 + mod/2^15, 32000/2^15),  h = h*dec + (1 - dec)*(x*dt*B).
 // The sum, 1 - dec (an FMA with -1: one rounding, as the subtraction) and the
-// three products are f32x2 operations, whose components round exactly as the
-// scalar ones; the final additions stay scalar, because an f32x2 add of two
-// f32x2 products is contracted into an f32x2 FMA by the compiler even with
-// -fmad=false, which would drop the rounding of one product.
+// products are f32x2 operations, whose components round exactly as the scalar
+// ones.  An f32x2 add of two f32x2 *products* is contracted into an f32x2 FMA
+// by the compiler even with -fmad=false (dropping one product's rounding), so
+// the two products of the final sum are written as FMAs with a +0 addend:
+// fma(a, b, +0) rounds a*b once, like the product, and the compiler leaves
+// the following f32x2 add alone (checked bitwise against the scalar form on
+// 4M random operands, and by the parity tests).  fma(a, b, +0) differs from
+// a*b only for an exact zero product of negative sign (+0 instead of -0), and
+// the sum h*dec + (1 - dec)*u can only see that when (1 - dec)*u is -0 too,
+// i.e. when B is -0.0: the model's x_proj output never is (an integer
+// accumulator times a positive scale), and a caller passing -0.0 in B may get
+// +0.0 where the reference keeps a -0.0 state -- the sign of a zero, nothing
+// else.
 __device__ __forceinline__ void state_pair_fast(float& h0, float& h1, float b0, float b1, float2 ms2, float2 xdt2,
                                                 float B0, float B1) {
     float2 dec = __fadd2_rn(make_float2(b0, b1), ms2);
@@ -282,10 +291,12 @@ __device__ __forceinline__ void state_pair_fast(float& h0, float& h1, float b0, 
     dec.y = min_nan(dec.y, 0.9765625f);
     const float2 om = __ffma2_rn(dec, make_float2(-1.0f, -1.0f), make_float2(1.0f, 1.0f));
     const float2 u = __fmul2_rn(xdt2, make_float2(B0, B1));
-    const float2 a1 = __fmul2_rn(make_float2(h0, h1), dec);
-    const float2 a2 = __fmul2_rn(om, u);
-    h0 = __fadd_rn(a1.x, a2.x);
-    h1 = __fadd_rn(a1.y, a2.y);
+    const float2 pz = make_float2(0.0f, 0.0f);
+    const float2 a1 = __ffma2_rn(make_float2(h0, h1), dec, pz);
+    const float2 a2 = __ffma2_rn(om, u, pz);
+    const float2 hn = __fadd2_rn(a1, a2);
+    h0 = hn.x;
+    h1 = hn.y;
 }
 
 // Inputs of the decay modulation: either the dt_proj output (RW == 0) or the
@@ -689,6 +700,9 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
                     float* __restrict__ amax, float* __restrict__ h_out, int L, int D) {
     __shared__ __align__(16) ScanStage ring[PIPE_NR];
     __shared__ unsigned fmask2[PIPE_NR][2];
+    // Fixed roles per warp index: the SM already places warp w of its k-th
+    // resident CTA on sub-partition (w + k) % 4 (measured), so the recurrence
+    // warps of co-resident CTAs land on different sub-partitions.
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.y;
     const int d0 = blockIdx.x * 32;
@@ -849,6 +863,9 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
         const int s = c % PIPE_NR;
         ScanStage& st = ring[s];
         unsigned fast_mask = 0;
+        // the four rows' decay modulations first, then their squareplus in two
+        // f32x2 pairs (squareplus_bounded2: the same roundings per element)
+        float modv[4], sqv[4];
 #pragma unroll
         for (int jj = 0; jj < 4; jj++) {
             const int j = 4 * hf + jj;
@@ -868,8 +885,19 @@ ssm_scan_pipe_kernel(const float* __restrict__ act, const float* __restrict__ bc
             } else {
                 mr = st.mod[j][lane];
             }
-            const float mod = ste_clamp(mr, -20.0f, 20.0f);
-            const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);
+            modv[jj] = ste_clamp(mr, -20.0f, 20.0f);
+        }
+#pragma unroll
+        for (int p = 0; p < 2; p++) {
+            const float2 sp = squareplus_bounded2(make_float2(modv[2 * p], modv[2 * p + 1]));
+            sqv[2 * p] = sp.x;
+            sqv[2 * p + 1] = sp.y;
+        }
+#pragma unroll
+        for (int jj = 0; jj < 4; jj++) {
+            const int j = 4 * hf + jj;
+            const float mod = modv[jj];
+            const float dtv = ste_clamp(__fmul_rn(sqv[jj], 0.01f), 0.001f, 0.1f);
             bool inside = (mod == 0.0f || fabsf(mod) >= 1e-30f);
             if (!wide_ok)
                 inside = inside && !bnan && (bmin >= 1.0f) && (__fadd_rn(bmin, mod) >= 0.0f) &&

@@ -44,18 +44,57 @@ def init_from_env(backend: str = "nccl", timeout_s: float = 120.0):
     return world, rank
 
 
+class LastLogitsGather:
+    """All-gather of every rank's last-position logits [b_rank, V] into
+    [global_batch, V] in global sequence order, with its buffers allocated once
+    (per call: one copy into the send buffer, one all_gather_into_tensor, and
+    for uneven shards one compaction copy per rank).
+
+    Shards may be uneven (``shard_counts``): each rank sends a buffer padded to
+    the largest shard, and the padding rows are dropped on the way out."""
+
+    def __init__(self, global_batch: int, vocab: int, dtype=torch.float32, device=None):
+        world = dist.get_world_size()
+        self.rank = dist.get_rank()
+        self.counts = shard_counts(global_batch, world)
+        self.mx = max(self.counts)
+        self.global_batch = global_batch
+        self.send = torch.zeros(self.mx, vocab, dtype=dtype, device=device)
+        self.recv = torch.empty(world * self.mx, vocab, dtype=dtype, device=device)
+        self.even = all(c == self.mx for c in self.counts)
+        self.out = self.recv if self.even else torch.empty(global_batch, vocab, dtype=dtype, device=device)
+
+    def __call__(self, local_last: torch.Tensor) -> torch.Tensor:
+        n = self.counts[self.rank]
+        if local_last.shape[0] != n:
+            raise ValueError(f"rank {self.rank} holds {local_last.shape[0]} rows, expected {n}")
+        self.send[:n].copy_(local_last)
+        dist.all_gather_into_tensor(self.recv, self.send)
+        if self.even:
+            return self.recv
+        o = 0
+        for r, c in enumerate(self.counts):
+            self.out[o:o + c].copy_(self.recv[r * self.mx: r * self.mx + c])
+            o += c
+        return self.out
+
+
 def gather_last_logits(local_last: torch.Tensor, global_batch: int) -> torch.Tensor:
     """All-gather every rank's last-position logits [b_rank, V] into [global_batch, V]
     in global sequence order (handles uneven shards by padding to the largest)."""
+    g = LastLogitsGather(global_batch, local_last.shape[1], local_last.dtype, local_last.device)
+    return g(local_last).clone()
+
+
+def gather_ids(local_ids: torch.Tensor, global_batch: int) -> torch.Tensor:
+    """All-gather every rank's generated token ids [b_rank, steps] (int64) into
+    [global_batch, steps] in global stream order (uneven shards padded)."""
     world = dist.get_world_size()
     counts = shard_counts(global_batch, world)
-    if local_last.shape[0] != counts[dist.get_rank()]:
-        raise ValueError(f"rank {dist.get_rank()} holds {local_last.shape[0]} rows, expected {counts[dist.get_rank()]}")
     mx = max(counts)
-    V = local_last.shape[1]
-    buf = torch.zeros(mx, V, dtype=local_last.dtype, device=local_last.device)
-    buf[: local_last.shape[0]] = local_last
-    out = torch.empty(world * mx, V, dtype=local_last.dtype, device=local_last.device)
+    steps = local_ids.shape[1]
+    buf = torch.zeros(mx, steps, dtype=local_ids.dtype, device=local_ids.device)
+    buf[: local_ids.shape[0]] = local_ids
+    out = torch.empty(world * mx, steps, dtype=local_ids.dtype, device=local_ids.device)
     dist.all_gather_into_tensor(out, buf)
-    parts = [out[r * mx: r * mx + counts[r]] for r in range(world)]
-    return torch.cat(parts, 0)
+    return torch.cat([out[r * mx: r * mx + counts[r]] for r in range(world)], 0)

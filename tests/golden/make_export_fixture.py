@@ -13,10 +13,10 @@ the logits the loaded model must reproduce.  Writes
   export_tiny.json   config, ids, sha256 of the logits and of every exported
                      array as the reference model holds it.
 
-Only runs where the reference checkout exists (default /root/reference, or
-$MI_REFERENCE_ROOT):
+Only runs where the reference checkout exists; $MI_REFERENCE_ROOT (required)
+names it:
 
-    python tests/golden/make_export_fixture.py
+    MI_REFERENCE_ROOT=<reference checkout> python tests/golden/make_export_fixture.py
 """
 from __future__ import annotations
 
@@ -59,7 +59,9 @@ def ids():
 
 
 def main() -> None:
-    ref_root = os.environ.get("MI_REFERENCE_ROOT", "/root/reference")
+    ref_root = os.environ.get("MI_REFERENCE_ROOT")
+    if not ref_root:
+        raise SystemExit("set MI_REFERENCE_ROOT to the reference checkout")
     sys.path.insert(0, os.path.join(ref_root, "src"))
     sys.path.insert(0, os.path.join(ref_root, "scripts"))
     import export_int8  # noqa: E402  (the reference exporter)

@@ -1,7 +1,8 @@
 """Generate the golden fixtures that pin the CPU oracle to the reference.
 
-Runs the UNMODIFIED reference CPU path (imported from the reference checkout,
-default /root/reference/src, or $MI_REFERENCE_SRC) on seeded inputs and writes
+Runs the UNMODIFIED reference CPU path (imported from the reference checkout
+named by $MI_REFERENCE_SRC, its src/ directory; required) on seeded inputs and
+writes
 
   model_<case>.json   sha256 of every hooked stage output and of the logits of
                       MambaIntegerModel.forward, plus a few raw logit values;
@@ -13,7 +14,7 @@ Inputs are regenerated from seeds by tests/golden/cases.py, so only outputs
 are stored.  The fixtures are committed; this script is only needed to
 regenerate them and only runs where the reference checkout exists.
 
-    python tests/golden/make_golden.py
+    MI_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -39,7 +40,9 @@ def sha(a) -> str:
 
 
 def _import_reference():
-    src = os.environ.get("MI_REFERENCE_SRC", "/root/reference/src")
+    src = os.environ.get("MI_REFERENCE_SRC")
+    if not src:
+        raise SystemExit("set MI_REFERENCE_SRC to the reference checkout's src/ directory")
     sys.path.insert(0, src)
     import mamba_integer_model as ref_model  # noqa: E402
     import rational_bitnet as ref_bitnet  # noqa: E402

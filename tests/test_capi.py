@@ -56,5 +56,11 @@ def test_host_side_argument_errors_need_no_gpu(lib):
     assert lib.mi_argmax_rows(None, 16, 1, 16, None, None) == -1
     # row conv: at most 4096 channels
     assert lib.mi_conv_act_quant_rows(p, 8200, p, p, p, p, p, 1, 8, 4100, None) == -2
+    # the allocation-free conv: one row above its fixed scratch (2^18 rows) is rejected before
+    # any CUDA call; xq and xscale are required
+    assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, p, 1, (1 << 18) + 1, 4, None) == -2
+    assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, p, 2, (1 << 17) + 1, 4, None) == -2
+    assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, None, p, 1, 8, 4, None) == -1
+    assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, None, 1, 8, 4, None) == -1
     assert lib.mi_version() >= 1
     assert lib.mi_status_string(-2) == b"unsupported shape or configuration"

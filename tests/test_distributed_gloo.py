@@ -31,6 +31,17 @@ def _worker(rank, world, port, global_batch, V, q):
     # each rank's "logits": row i of the global batch holds value i in every column
     local = torch.arange(lo, hi, dtype=torch.float32).unsqueeze(1).repeat(1, V)
     full = mdist.gather_last_logits(local, global_batch)
+    # the reusable gather bench.py times: twice with the same buffers, fed a strided view
+    # (the last position of [b, L, V] logits) as the prefill engine's output is
+    g = mdist.LastLogitsGather(global_batch, V)
+    seq = torch.zeros(hi - lo, 3, V)
+    for step in range(2):
+        seq[:, -1, :] = local + 1000 * step
+        got = g(seq[:, -1, :])
+        assert got.shape == (global_batch, V)
+        assert got[:, 0].tolist() == [float(i + 1000 * step) for i in range(global_batch)]
+    ids = mdist.gather_ids(torch.arange(lo, hi, dtype=torch.int64).unsqueeze(1).repeat(1, 2), global_batch)
+    assert ids[:, 1].tolist() == list(range(global_batch))
     q.put((rank, (lo, hi), full[:, 0].tolist()))
     dist.barrier()
     dist.destroy_process_group()

@@ -53,6 +53,30 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda_dev):
         assert torch.equal(xs.view(torch.int32), xs_r.view(torch.int32)), f"call {call}: scales differ"
 
 
+def test_noalloc_accepts_exactly_its_row_limit(cuda_dev):
+    # batch * L == 262144, the size of the fixed scratch: accepted, same bits as the workspace entry point
+    from mamba_integer_b200 import _lib
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    bsz, L, D = 2, 1 << 17, 4
+    T = bsz * L
+    xz, w, b = _inputs(7, 3.0, bsz, L, D, cuda_dev)
+    act_r, xq_r, xs_r = _outputs(T, D, cuda_dev)
+    ws = torch.empty(T, device=cuda_dev)
+    _lib.check(lib.mi_conv_act_quant(xz.data_ptr(), xz.stride(0), w.data_ptr(), b.data_ptr(), act_r.data_ptr(),
+                                     xq_r.data_ptr(), xs_r.data_ptr(), ws.data_ptr(), bsz, L, D, stream),
+               "mi_conv_act_quant")
+    act, xq, xs = _outputs(T, D, cuda_dev)
+    _lib.check(lib.mi_conv_act_quant_noalloc(xz.data_ptr(), xz.stride(0), w.data_ptr(), b.data_ptr(), act.data_ptr(),
+                                             xq.data_ptr(), xs.data_ptr(), bsz, L, D, stream),
+               "mi_conv_act_quant_noalloc")
+    torch.cuda.synchronize()
+    assert torch.equal(act.view(torch.int32), act_r.view(torch.int32))
+    assert torch.equal(xq, xq_r)
+    assert torch.equal(xs.view(torch.int32), xs_r.view(torch.int32))
+
+
 def test_noalloc_rejects_more_rows_than_its_scratch(cuda_dev):
     from mamba_integer_b200 import _lib
 
@@ -61,3 +85,5 @@ def test_noalloc_rejects_more_rows_than_its_scratch(cuda_dev):
     p = dummy.data_ptr()
     rc = lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, p, 1 << 10, 1 << 10, 8, ctypes.c_void_p(0))
     assert rc == -2  # MI_ERR_UNSUPPORTED: batch * L above the fixed maximum, nothing launched
+    rc = lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, p, 1, (1 << 18) + 1, 4, ctypes.c_void_p(0))
+    assert rc == -2  # one row above the limit
