@@ -76,13 +76,13 @@ int mi_bitshift_norm(const float* x, const float* gamma, const float* step, floa
  *   xscale = s / 127.
  * x [T, >=K] row stride ldx; xq [T, >=K] row stride ldq (int8).
  * amax (optional, [T]): max|x| of each row already computed by the producer
- * of x (NULL: computed here); it is consumed: each entry is read and then
- * reset to 0, so a producer that accumulates row maxima by atomicMax (the
- * fused scan) can reuse the array on the next call without a separate fill.
+ * of x (NULL: computed here).  clear (optional, [T]): set to 0 by this call,
+ * row for row -- the row-maximum array of a kernel that follows and
+ * accumulates by atomicMax (the fused scan), without a separate fill.
  * Replaces: fast_quantize_activations, src/triton_kernels/bitnet_kernels.py:98.
  */
 int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
-                     float* amax, void* stream);
+                     const float* amax, float* clear, void* stream);
 
 /*
  * Row pre-pass in front of a BitLinear: optional residual update, BitShiftNorm,
@@ -145,6 +145,29 @@ int mi_bitlinear_packed(const int8_t* A, int lda, const uint8_t* Wp, const float
                         int N, int K, int epilogue, void* stream);
 
 /*
+ * BitLinear with the BitShift-norm + squareplus epilogue of BASELINE config 3
+ * (2-bit packed ternary weights).  acc [M, N] int32 (row stride ldc) receives
+ * the exact accumulators; out [M, N] fp32 (row stride ldo) receives, per row,
+ *   y = acc * (w_scale * a_scale[m]);  BitShiftNorm of y with the mean and the
+ *   power-of-two variance scale taken exactly from the integer row sums
+ *   S1 = sum acc, S2 = sum acc^2;  o = ((y - mean) * s * gamma[n]) * step;
+ *   out = squareplus(ste_clamp(o, -50, 50)).
+ * (The reference has no fused GEMM + norm: this chains its stages, and
+ * defines the statistics from exact integers so that they do not depend on
+ * a summation order; the restatement is oracle/mi_oracle.c:orc_bitlinear_norm_sqp.)
+ * gamma [N] and step [1] are device pointers.  stats_ws: caller workspace of
+ * 2*M uint64 (S1, S2 per row, zeroed by the call).  K % 64 == 0,
+ * N % 16 == 0, N*K <= 2^24; acc, out, gamma 16-byte aligned.
+ * Replaces the chain BitLinear.forward (src/rational_bitnet.py:204-208) ->
+ * BitShiftNorm (src/mamba_integer_model.py:199-222) -> fused_squareplus_clamp
+ * (src/triton_kernels/fused_activations.py:229) on one row of outputs.
+ */
+int mi_bitlinear_packed_norm_sqp(const int8_t* A, int lda, const uint8_t* Wp, const float* a_scale,
+                                 const float* w_scale, const float* gamma, const float* step, int32_t* acc,
+                                 int ldc, float* out, int ldo, uint64_t* stats_ws, int M, int N, int K,
+                                 void* stream);
+
+/*
  * Causal depthwise conv (4 taps, bias first then one FMA per tap) +
  * ste_clamp(-50, 50) + squareplus (3 Newton steps), then int8 quantisation of
  * each row of the activation.
@@ -191,7 +214,8 @@ int mi_conv_act_quant_noalloc(const float* xz, int ldx, const float* w, const fl
  * act [batch*L, D]; bc rows (stride ldbc): B at [0,N), C at [N,2N);
  * modraw [batch*L, D]; z rows stride ldz; base [D,N]; y [batch*L, D].
  * amax (optional, [batch*L], zero on entry) receives max|y| per row (feed it
- * to mi_quantize_rows, which resets it to zero).
+ * to mi_quantize_rows; the quantisation of the dt rows that precedes the scan
+ * can clear it).
  * N == 16.  Results are the reference's bits; the one exception is the sign
  * of a zero: where B holds -0.0 (the model's x_proj output never does), a
  * state the reference leaves at -0.0 may come out +0.0.

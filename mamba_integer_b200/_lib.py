@@ -30,11 +30,12 @@ SIGNATURES = {
     "mi_device_error": [ctypes.POINTER(ctypes.c_int), _i, _p],
     "mi_scan_i32": [_p, _p, _p, _p, _i, _p, _p, _p, _i, _i, _i, _i, _p],
     "mi_bitshift_norm": [_p, _p, _p, _p, _p, _i, _i, _i, _p],
-    "mi_quantize_rows": [_p, _i, _i, _i, _p, _i, _p, _p, _p],
+    "mi_quantize_rows": [_p, _i, _i, _i, _p, _i, _p, _p, _p, _p],
     "mi_rowprep": [_p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mi_bitlinear_i8": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_pack_ternary": [_p, _i, _p, _i, _i, _p],
     "mi_bitlinear_packed": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
+    "mi_bitlinear_packed_norm_sqp": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _i, _i, _p],
     "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_conv_act_quant_noalloc": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_conv_act_quant_rows": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],

@@ -226,7 +226,8 @@ template <int BN, bool PACKED>
 __global__ void __launch_bounds__(threads_of<PACKED>(), 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
-               const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K, int epi) {
+               const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K, int epi,
+               unsigned long long* __restrict__ row_stats) {
     using C = Cfg<BN, PACKED>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
@@ -397,6 +398,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             float sc = 0.0f;
             if (epi == MI_EPI_F32_SCALED && row < M) sc = __fmul_rn(ws, a_scale[row]);  // (w_scale * x_scale)
             const uint32_t tacc = tmem + (uint32_t)(a * C::TMEM_COLS) + ((uint32_t)(q * 32) << 16);
+            long long s1 = 0, s2 = 0;  // exact row sums of this tile's accumulators (row_stats)
 #pragma unroll 1
             for (int cb = 0; cb < C::EPI_BOXES; cb++, nst++) {
                 uint32_t r[32] = {};
@@ -408,6 +410,15 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(tempty_bar(a)) : "memory");
+                }
+                if (row_stats) {
+                    // columns past N hold 0 (their weight rows were filled with zeros by the TMA)
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const long long v = (int32_t)r[j];
+                        s1 += v;
+                        s2 += v * v;
+                    }
                 }
                 if (epi == MI_EPI_F32_SCALED) {
 #pragma unroll
@@ -435,6 +446,11 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     if (x < N && y < M) tma_store_2d(&tmC, stg + (nst & (C::STG_BUFS - 1)) * 4096, x, y);
                     asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
                 }
+            }
+            if (row_stats && row < M) {
+                // two's complement: the unsigned 64-bit adds accumulate signed sums exactly
+                atomicAdd(row_stats + 2 * (size_t)row, (unsigned long long)s1);
+                atomicAdd(row_stats + 2 * (size_t)row + 1, (unsigned long long)s2);
             }
         }
         if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
@@ -795,7 +811,8 @@ static int make_wmap(CUtensorMap* tm, const void* W, int N, int K, int box_rows)
 
 template <int BN, bool PACKED>
 static int launch(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
-                  const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
+                  const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s,
+                  unsigned long long* row_stats = nullptr) {
     // a tile whose last 32-column box sticks out past BN would overwrite the next tile
     if ((BN % 32) != 0 && N > BN) return MI_ERR_UNSUPPORTED;
     CUtensorMap ta, tb, tc;
@@ -819,7 +836,7 @@ static int launch(const int8_t* A, int lda, const void* W, const float* a_scale,
     const int tiles = cdiv(M, BM) * cdiv(N, BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
     gemm_i8_kernel<BN, PACKED><<<grid, threads_of<PACKED>(), C::SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale,
-                                                                         M, N, K, epi);
+                                                                         M, N, K, epi, row_stats);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }
@@ -944,6 +961,136 @@ extern "C" int mi_pack_ternary(const int8_t* W, int ldw, uint8_t* Wp, int N, int
         W, ldw, reinterpret_cast<uint32_t*>(Wp), N, K);
     MI_CHECK_LAUNCH();
     return MI_OK;
+}
+
+namespace mi {
+namespace gemm {
+
+// ---------------------------------------------------------------------------
+// BitLinear + BitShift norm + squareplus (BASELINE config 3's epilogue).
+//
+// The norm of an output row needs statistics of the whole row (8192 columns
+// at config 3 = 32 tiles of 256), which no single tile's epilogue sees.  Two
+// passes:
+//   1. the GEMM (gemm_i8_kernel with row_stats) writes the int32 accumulators
+//      and, per tile, adds each row's exact sums S1 = sum acc and
+//      S2 = sum acc^2 (int64) into a caller workspace by atomics -- integer
+//      sums, so their value does not depend on the tile order;
+//   2. norm_sqp_rows_kernel, one warp per row, turns S1, S2 into the mean and
+//      the power-of-two scale (double arithmetic on exact integers, each
+//      operation rounded once) and streams the row once: dequantise, centre,
+//      scale, gamma, step, ste_clamp(-50, 50), squareplus -> fp32.
+// The definition (no reference function fuses these stages) is restated in
+// oracle/mi_oracle.c:orc_bitlinear_norm_sqp.
+// ---------------------------------------------------------------------------
+
+// _find_power_of_2_scale's threshold table (src/mamba_integer_model.py:144-184)
+// on a double argument that already includes the 1e-9.
+__device__ __forceinline__ float pow2_scale_d(double v) {
+    float s = 1.0f;
+    if (v >= 4.0) s = 0.5f;
+    if (v >= 16.0) s = 0.25f;
+    if (v >= 64.0) s = 0.125f;
+    if (v >= 256.0) s = 0.0625f;
+    if (v >= 1024.0) s = 0.03125f;
+    if (v >= 4096.0) s = 0.015625f;
+    if (v >= 16384.0) s = 0.0078125f;
+    if (v >= 65536.0) s = 0.00390625f;
+    if (v < 1.0) s = 1.0f;
+    if (v < 0.25) s = 2.0f;
+    if (v < 0.0625) s = 4.0f;
+    if (v < 0.015625) s = 8.0f;
+    return s;
+}
+
+__device__ __forceinline__ float norm_elem(int32_t a, float sc, float mean, float s, float g, float st) {
+    const float y = __fmul_rn(__int2float_rn(a), sc);
+    const float xc = __fsub_rn(y, mean);
+    return ste_clamp(__fmul_rn(__fmul_rn(__fmul_rn(xc, s), g), st), -50.0f, 50.0f);
+}
+
+__global__ void __launch_bounds__(256)
+norm_sqp_rows_kernel(const int32_t* __restrict__ acc, int ldc, const unsigned long long* __restrict__ stats,
+                     const float* __restrict__ a_scale, const float* __restrict__ w_scale,
+                     const float* __restrict__ gamma, const float* __restrict__ step, float* __restrict__ out,
+                     int ldo, int M, int N) {
+    const int lane = threadIdx.x & 31;
+    const int warps = blockDim.x >> 5;
+    const float ws = *w_scale, st = *step;
+    for (int m = blockIdx.x * warps + (threadIdx.x >> 5); m < M; m += gridDim.x * warps) {
+        const long long s1 = (long long)stats[2 * (size_t)m], s2 = (long long)stats[2 * (size_t)m + 1];
+        const float sc = __fmul_rn(ws, a_scale[m]);  // (w_scale * x_scale), as the BitLinear rescale
+        const double dsc = (double)sc;
+        const float mean = __double2float_rn(__dmul_rn(__ddiv_rn(__ll2double_rn(s1), (double)N), dsc));
+        const long long vnum = (long long)N * s2 - s1 * s1;  // >= 0, < 2^62 for N*K <= 2^24
+        const double var = __dmul_rn(__ddiv_rn(__ll2double_rn(vnum), __dmul_rn((double)N, (double)N)),
+                                     __dmul_rn(dsc, dsc));
+        const float s = pow2_scale_d(__dadd_rn(var, (double)1e-9f));
+        const int32_t* row = acc + (size_t)m * ldc;
+        float* orow = out + (size_t)m * ldo;
+        for (int c = 4 * lane; c < N; c += 128) {
+            const int4 a = *reinterpret_cast<const int4*>(row + c);
+            const float4 g = *reinterpret_cast<const float4*>(gamma + c);
+            // ste_clamp results (not f32x2 products) feed the paired squareplus
+            const float2 p = squareplus_bounded2(make_float2(norm_elem(a.x, sc, mean, s, g.x, st),
+                                                             norm_elem(a.y, sc, mean, s, g.y, st)));
+            const float2 q = squareplus_bounded2(make_float2(norm_elem(a.z, sc, mean, s, g.z, st),
+                                                             norm_elem(a.w, sc, mean, s, g.w, st)));
+            *reinterpret_cast<float4*>(orow + c) = make_float4(p.x, p.y, q.x, q.y);
+        }
+    }
+}
+
+static int bitlinear_norm_sqp(const int8_t* A, int lda, const uint8_t* Wp, const float* a_scale,
+                              const float* w_scale, const float* gamma, const float* step, int32_t* acc, int ldc,
+                              float* out, int ldo, unsigned long long* stats_ws, int M, int N, int K,
+                              cudaStream_t s) {
+    if (!A || !Wp || !a_scale || !w_scale || !gamma || !step || !acc || !out || !stats_ws) return MI_ERR_INVALID;
+    if (M <= 0 || N <= 0 || K <= 0) return MI_ERR_INVALID;
+    if (K % 64 != 0 || lda < K || lda % 16 != 0 || N % 16 != 0) return MI_ERR_UNSUPPORTED;
+    if ((long long)N * K > (1LL << 24)) return MI_ERR_UNSUPPORTED;  // keeps N*S2 and S1^2 below 2^62
+    if (ldc < N || ldc % 4 != 0 || ldo < N || ldo % 4 != 0) return MI_ERR_INVALID;
+    if ((((uintptr_t)A) | ((uintptr_t)Wp) | ((uintptr_t)acc) | ((uintptr_t)out) | ((uintptr_t)gamma)) & 15)
+        return MI_ERR_INVALID;
+    if (((uintptr_t)stats_ws) & 7) return MI_ERR_INVALID;
+    if (cudaMemsetAsync(stats_ws, 0, sizeof(unsigned long long) * 2 * (size_t)M, s) != cudaSuccess) {
+        cudaGetLastError();
+        return MI_ERR_CUDA;
+    }
+    const int sms = sm_count();
+    const long long tm = cdiv(M, BM);
+    auto fills = [&](int bn) { return tm * cdiv(N, bn) >= sms; };
+    int rc;
+    // the streaming kernel (whose epilogue adds the row sums), widest tile that fills the SMs
+    if (N <= 32) rc = launch<32, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else if (N <= 64) rc = launch<64, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else if (N <= 96) rc = launch<96, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else if (N % 256 == 0 && fills(256))
+        rc = launch<256, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else if (N <= 128 || fills(128))
+        rc = launch<128, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else if (fills(64))
+        rc = launch<64, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else
+        rc = launch<32, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    if (rc != MI_OK) return rc;
+    int blocks = cdiv(M, 8);
+    if (blocks > sms * 16) blocks = sms * 16;
+    norm_sqp_rows_kernel<<<blocks, 256, 0, s>>>(acc, ldc, stats_ws, a_scale, w_scale, gamma, step, out, ldo, M, N);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+}  // namespace gemm
+}  // namespace mi
+
+extern "C" int mi_bitlinear_packed_norm_sqp(const int8_t* A, int lda, const uint8_t* Wp, const float* a_scale,
+                                            const float* w_scale, const float* gamma, const float* step,
+                                            int32_t* acc, int ldc, float* out, int ldo, uint64_t* stats_ws, int M,
+                                            int N, int K, void* stream) {
+    return mi::gemm::bitlinear_norm_sqp(A, lda, Wp, a_scale, w_scale, gamma, step, acc, ldc, out, ldo,
+                                        reinterpret_cast<unsigned long long*>(stats_ws), M, N, K,
+                                        (cudaStream_t)stream);
 }
 
 extern "C" int mi_bitlinear_packed(const int8_t* A, int lda, const uint8_t* Wp, const float* a_scale,

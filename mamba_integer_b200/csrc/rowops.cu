@@ -157,7 +157,7 @@ rowprep_kernel(const float* x, const float* delta, const float* __restrict__ res
 // absmax, then quantise; the second pass re-reads the row from L1/L2).
 __global__ void __launch_bounds__(256)
 quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __restrict__ xq, int ldq,
-                  float* __restrict__ xscale, float* __restrict__ amax_in) {
+                  float* __restrict__ xscale, const float* __restrict__ amax_in, float* __restrict__ clear) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
     for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
@@ -178,13 +178,10 @@ quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __
         float sc = clamp_t(amax, 1e-8f, __int_as_float(0x7f800000));
         float inv = __fmul_rn(__frcp_rn(sc), 127.0f);
         for (int k = lane; k < K; k += 32) xq[(size_t)t * ldq + k] = (int8_t)quant_i8(__fmul_rn(row[k], inv));
-        if (amax_in) {
-            // every lane has read the row's maximum: reset it to zero, so that a producer
-            // accumulating it by atomicMax can reuse the array without a fill
-            __syncwarp();
-            if (lane == 0) amax_in[t] = 0.0f;
+        if (lane == 0) {
+            xscale[t] = __fdiv_rn(sc, 127.0f);
+            if (clear) clear[t] = 0.0f;
         }
-        if (lane == 0) xscale[t] = __fdiv_rn(sc, 127.0f);
     }
 }
 
@@ -194,7 +191,7 @@ quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __
 // absmax and NaN flag reduced over its 16 lanes.
 __global__ void __launch_bounds__(256)
 quant_rows_narrow_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __restrict__ xq, int ldq,
-                         float* __restrict__ xscale) {
+                         float* __restrict__ xscale, float* __restrict__ clear) {
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int rows_per_cta = (blockDim.x >> 5) * 2;
@@ -223,7 +220,10 @@ quant_rows_narrow_kernel(const float* __restrict__ x, int ldx, int T, int K, int
             const int k = 4 * hl + e;
             if (okr && k < K) xq[(size_t)t * ldq + k] = (int8_t)quant_i8(__fmul_rn(v[e], inv));
         }
-        if (okr && hl == 0) xscale[t] = __fdiv_rn(sc, 127.0f);
+        if (okr && hl == 0) {
+            xscale[t] = __fdiv_rn(sc, 127.0f);
+            if (clear) clear[t] = 0.0f;
+        }
     }
 }
 
@@ -298,7 +298,7 @@ extern "C" int mi_rowprep(const float* x, const float* delta, const float* res_g
 }
 
 extern "C" int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* xq, int ldq, float* xscale,
-                                float* amax, void* stream) {
+                                const float* amax, float* clear, void* stream) {
     if (!x || !xq || !xscale) return MI_ERR_INVALID;
     if (T < 0 || K <= 0 || ldx < K || ldq < K) return MI_ERR_INVALID;
     if (T == 0) return MI_OK;
@@ -307,13 +307,14 @@ extern "C" int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* x
         int blocks = mi::cdiv(T, threads / 16);
         if (blocks > 148 * 16) blocks = 148 * 16;
         mi::rowops::quant_rows_narrow_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq,
-                                                                                           xscale);
+                                                                                           xscale, clear);
         MI_CHECK_LAUNCH();
         return MI_OK;
     }
     int blocks = mi::cdiv(T, threads / 32);
     if (blocks > 148 * 16) blocks = 148 * 16;
-    mi::rowops::quant_rows_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq, xscale, amax);
+    mi::rowops::quant_rows_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq, xscale, amax,
+                                                                                clear);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

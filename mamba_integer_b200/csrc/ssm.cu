@@ -1188,7 +1188,7 @@ extern "C" int mi_conv_act_quant(const float* xz, int ldx, const float* w, const
     mi::ssm::conv_act_kernel<<<grid, mi::ssm::CONV_THREADS, 0, s>>>(
         xz, ldx, w, bias, act, reinterpret_cast<unsigned int*>(amax_ws), L, D);
     MI_CHECK_LAUNCH();
-    if (xq) return mi_quantize_rows(act, D, T, D, xq, D, xscale, amax_ws, stream);
+    if (xq) return mi_quantize_rows(act, D, T, D, xq, D, xscale, amax_ws, nullptr, stream);
     return MI_OK;
 }
 

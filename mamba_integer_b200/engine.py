@@ -45,8 +45,8 @@ class _Workspace:
         self.dts = torch.empty(T, dtype=f32, device=dev)
         self.y = torch.empty(T, di, dtype=f32, device=dev)
         self.out = torch.empty(T, d, dtype=f32, device=dev)
-        # row maxima of the scan output: zero on entry to every scan (quant_y resets them)
-        self.amax = torch.zeros(T, dtype=f32, device=dev)
+        # row maxima of the scan output (zero-filled by the dt quantisation before each scan)
+        self.amax = torch.empty(T, dtype=f32, device=dev)
 
 
 def _layer_params(blk, dev):
@@ -101,10 +101,10 @@ def _ssm_half(p, ws: _Workspace, batch: int, L: int, d: int, di: int, R: int, N:
     with timer("gemm_x_proj"):
         ternary_matmul(ws.xq_i, p["w_x"], ws.xs_i, out=ws.xp)
     with timer("quant_dt"):
-        kernels.quantize_rows(ws.xp, K=R, out=ws.dtq, xscale=ws.dts)
+        kernels.quantize_rows(ws.xp, K=R, out=ws.dtq, xscale=ws.dts, clear=ws.amax)
     with timer("ssm_scan"):
-        # dt_proj is fused into the scan (each channel's dot product by dp4a); ws.amax is
-        # zero here: zero-filled at allocation and reset by the quantisation that reads it
+        # dt_proj is fused into the scan (each channel's dot product by dp4a); ws.amax was
+        # zero-filled by the dt quantisation just before
         kernels.ssm_scan_dt(ws.act, ws.xp[:, R:], ws.dtq, ws.dts, p["w_dt"].w8, p["w_dt"].scale, R, ws.xz[:, di:],
                             p["base"], batch, L, y=ws.y, amax=ws.amax, split=scan_split, h_out=h_out)
     with timer("quant_y"):

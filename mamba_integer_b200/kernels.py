@@ -90,10 +90,12 @@ def bitshift_norm(x: torch.Tensor, gamma: torch.Tensor, step, center_once: bool 
 
 
 def quantize_rows(x: torch.Tensor, K: Optional[int] = None, out: Optional[torch.Tensor] = None,
-                  xscale: Optional[torch.Tensor] = None, amax: Optional[torch.Tensor] = None
-                  ) -> Tuple[torch.Tensor, torch.Tensor]:
+                  xscale: Optional[torch.Tensor] = None, amax: Optional[torch.Tensor] = None,
+                  clear: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """Per-row absmax int8 quantisation of the first K columns of a 2-D fp32
-    tensor (row stride taken from x); returns (xq int8 [T, ldq], x_scale [T])."""
+    tensor (row stride taken from x); returns (xq int8 [T, ldq], x_scale [T]).
+    ``clear`` (fp32 [T], optional) is zero-filled on the way (the row maxima
+    the fused scan accumulates next)."""
     if x.dim() != 2 or x.stride(1) != 1:
         raise ValueError("x must be 2-D with unit column stride")
     _need(x, torch.float32, "x", contiguous=False)
@@ -103,8 +105,13 @@ def quantize_rows(x: torch.Tensor, K: Optional[int] = None, out: Optional[torch.
         out = torch.empty(T, K, dtype=torch.int8, device=x.device)
     if xscale is None:
         xscale = torch.empty(T, dtype=torch.float32, device=x.device)
+    if clear is not None:
+        _need(clear, torch.float32, "clear")
+        if clear.numel() < T:
+            raise ValueError("clear must hold one float per row")
     _lib.check(_lib.load().mi_quantize_rows(x.data_ptr(), x.stride(0), T, K, out.data_ptr(), out.stride(0),
-                                            xscale.data_ptr(), _ptr(amax), _stream()), "mi_quantize_rows")
+                                            xscale.data_ptr(), _ptr(amax), _ptr(clear), _stream()),
+               "mi_quantize_rows")
     return out, xscale
 
 
@@ -187,6 +194,36 @@ def bitlinear_packed(A: torch.Tensor, Wp: torch.Tensor, a_scale: Optional[torch.
 # ---------------------------------------------------------------------------
 # conv / scan / element-wise
 # ---------------------------------------------------------------------------
+def bitlinear_packed_norm_sqp(A: torch.Tensor, Wp: torch.Tensor, a_scale: torch.Tensor, w_scale: torch.Tensor,
+                              gamma: torch.Tensor, step: torch.Tensor, acc: Optional[torch.Tensor] = None,
+                              out: Optional[torch.Tensor] = None, stats_ws: Optional[torch.Tensor] = None
+                              ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Config 3's BitLinear + BitShift norm + squareplus (mi_bitlinear_packed_norm_sqp):
+    returns (acc int32 [M, N], out fp32 [M, N]).  stats_ws: int64 [M, 2] workspace."""
+    _need(Wp, torch.uint8, "Wp")
+    if A.dim() != 2 or A.stride(1) != 1:
+        raise ValueError("A must be 2-D with unit column stride")
+    _need(A, torch.int8, "A", contiguous=False)
+    for t, nm in ((a_scale, "a_scale"), (w_scale, "w_scale"), (gamma, "gamma"), (step, "step")):
+        _need(t, torch.float32, nm)
+    M, N, K = A.shape[0], Wp.shape[0], 4 * Wp.shape[1]
+    if acc is None:
+        acc = torch.empty(M, N, dtype=torch.int32, device=A.device)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32, device=A.device)
+    if stats_ws is None:
+        stats_ws = torch.empty(M, 2, dtype=torch.int64, device=A.device)
+    _need(acc, torch.int32, "acc", contiguous=False)
+    _need(out, torch.float32, "out", contiguous=False)
+    _need(stats_ws, torch.int64, "stats_ws")
+    _lib.check(_lib.load().mi_bitlinear_packed_norm_sqp(A.data_ptr(), A.stride(0), Wp.data_ptr(), a_scale.data_ptr(),
+                                                        w_scale.data_ptr(), gamma.data_ptr(), step.data_ptr(),
+                                                        acc.data_ptr(), acc.stride(0), out.data_ptr(), out.stride(0),
+                                                        stats_ws.data_ptr(), M, N, K, _stream()),
+               "mi_bitlinear_packed_norm_sqp")
+    return acc, out
+
+
 def conv_act_quant(xz: torch.Tensor, w: torch.Tensor, bias: torch.Tensor, batch: int, L: int, D: int,
                    act=None, xq=None, xscale=None, quantize: bool = True, amax_ws=None):
     """Causal depthwise conv + ste_clamp + squareplus (+ int8 quantisation) of

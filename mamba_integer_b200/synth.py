@@ -133,3 +133,12 @@ def bitlinear_inputs(M=16384, K=2048, N=8192, seed=2):
     Wf = ternary_weight(N, K, g, e=5)  # mean|W| = 2^-6
     Wq = (Wf * 32.0).to(torch.int8)
     return A, a_scale, Wq, 2.0 ** -6
+
+
+def bitlinear_norm_params(N=8192, seed=2):
+    """Config 3's epilogue parameters: BitShiftNorm gain gamma [N] = 1 + 0.1 N(0, 1)
+    and step size 0.875 (the reference initialises both to 1; non-trivial values
+    exercise the multiplications)."""
+    g = torch.Generator().manual_seed(seed + 100)
+    gamma = 1.0 + 0.1 * torch.randn(N, generator=g)
+    return gamma.to(torch.float32), torch.tensor([0.875], dtype=torch.float32)

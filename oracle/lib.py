@@ -54,6 +54,9 @@ def _load():
     lib.orc_pack_ternary.argtypes = [_i8p, _i64, _i64, _u8p]
     lib.orc_unpack_ternary.restype = None
     lib.orc_unpack_ternary.argtypes = [_u8p, _i64, _i64, _i8p]
+    lib.orc_bitlinear_norm_sqp.restype = None
+    lib.orc_bitlinear_norm_sqp.argtypes = [_i32p, _f32p, ctypes.c_float, _f32p, ctypes.c_float, _f32p, _i64p, _i64,
+                                           _i64, ctypes.c_int]
     lib.orc_gemm_i8_i32.restype = None
     lib.orc_gemm_i8_i32.argtypes = [_i8p, _i8p, _i32p, _i64, _i64, _i64, ctypes.c_int]
     lib.orc_conv_sqp.restype = None
@@ -166,6 +169,20 @@ def gemm_i8_i32(A, W, nthreads=0):
     C = np.empty((M, N), np.int32)
     _load().orc_gemm_i8_i32(_p(A, _i8p), _p(W, _i8p), _p(C, _i32p), M, N, K, nthreads)
     return C
+
+
+def bitlinear_norm_sqp(acc, a_scale, w_scale, gamma, step, nthreads=0):
+    """Config-3 epilogue on int32 accumulators [M, N]: (out fp32 [M, N], stats int64 [M, 2])."""
+    acc = _c(acc, np.int32)
+    M, N = acc.shape
+    a_scale = _c(a_scale, np.float32)
+    gamma = _c(gamma, np.float32)
+    out = np.empty((M, N), np.float32)
+    stats = np.empty((M, 2), np.int64)
+    _load().orc_bitlinear_norm_sqp(_p(acc, _i32p), _p(a_scale, _f32p), float(np.float32(w_scale)),
+                                   _p(gamma, _f32p), float(np.float32(step)), _p(out, _f32p), _p(stats, _i64p), M,
+                                   N, nthreads)
+    return out, stats
 
 
 def conv_sqp(x, w, bias, nthreads=0):

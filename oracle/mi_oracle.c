@@ -285,6 +285,78 @@ void orc_bitlinear(const int8_t* xq, int64_t ldq, const float* xscale, int64_t T
     }
 }
 
+/* _find_power_of_2_scale's threshold table (src/mamba_integer_model.py:144-184)
+ * on a double argument that already includes the 1e-9. */
+static inline float pow2_scale_d(double v) {
+    float s = 1.0f;
+    if (v >= 4.0) s = 0.5f;
+    if (v >= 16.0) s = 0.25f;
+    if (v >= 64.0) s = 0.125f;
+    if (v >= 256.0) s = 0.0625f;
+    if (v >= 1024.0) s = 0.03125f;
+    if (v >= 4096.0) s = 0.015625f;
+    if (v >= 16384.0) s = 0.0078125f;
+    if (v >= 65536.0) s = 0.00390625f;
+    if (v < 1.0) s = 1.0f;
+    if (v < 0.25) s = 2.0f;
+    if (v < 0.0625) s = 4.0f;
+    if (v < 0.015625) s = 8.0f;
+    return s;
+}
+
+/*
+ * BitLinear epilogue of BASELINE config 3: BitShift norm + squareplus of each
+ * output row, statistics taken exactly from the int32 accumulators.  The
+ * reference has no fused GEMM + norm; this chains its stages on the BitLinear
+ * output y = acc * (w_scale * a_scale[m]) (src/rational_bitnet.py:204-208):
+ * BitShiftNorm (src/mamba_integer_model.py:199-222: centre, variance, the
+ * power-of-two scale of _find_power_of_2_scale :144-184, ((x_c*s)*gamma)*step),
+ * then ste_clamp(-50, 50) and _squareplus_rational (:410-411, :114-121).
+ *
+ * The reference's fp32 mean and variance depend on its summation order, which
+ * a tiled GPU reduction cannot follow, so this build defines them from the
+ * exact integer sums S1 = sum acc and S2 = sum acc^2 (int64; N*K <= 2^24 keeps
+ * N*S2 and S1^2 below 2^62), with sc = fl(w_scale * a_scale[m]):
+ *   mean = (float)((S1 / (double)N) * (double)sc)
+ *   var  = ((double)(N*S2 - S1*S1) / ((double)N * N)) * ((double)sc * sc)
+ *   s    = pow2 table on var + 1e-9 (double; each double operation rounded once)
+ * and one centring (the second centring of BitShiftNormFunction subtracts the
+ * mean of an exactly centred row, i.e. zero).  Per element, in fp32:
+ *   y = (float)acc * sc;  x_c = y - mean;  o = ((x_c * s) * gamma[n]) * step;
+ *   out = squareplus(ste_clamp(o, -50, 50)).
+ * stats_out (optional, [M, 2] int64) receives S1, S2.
+ */
+void orc_bitlinear_norm_sqp(const int32_t* acc, const float* a_scale, float w_scale, const float* gamma, float step,
+                            float* out, int64_t* stats_out, int64_t M, int64_t N, int nthreads) {
+#pragma omp parallel for schedule(static) ORC_THREADS(nthreads)
+    for (int64_t m = 0; m < M; m++) {
+        const int32_t* r = acc + m * N;
+        int64_t s1 = 0, s2 = 0;
+        for (int64_t n = 0; n < N; n++) {
+            s1 += r[n];
+            s2 += (int64_t)r[n] * r[n];
+        }
+        if (stats_out) {
+            stats_out[2 * m] = s1;
+            stats_out[2 * m + 1] = s2;
+        }
+        const float sc = w_scale * a_scale[m];
+        const double dsc = (double)sc;
+        const float mean = (float)(((double)s1 / (double)N) * dsc);
+        const int64_t vnum = N * s2 - s1 * s1;
+        const double var = ((double)vnum / ((double)N * (double)N)) * (dsc * dsc);
+        const float s = pow2_scale_d(var + (double)1e-9f);
+        for (int64_t n = 0; n < N; n++) {
+            const float y = (float)r[n] * sc;
+            const float xc = y - mean;
+            float o = xc * s;
+            o = o * gamma[n];
+            o = o * step;
+            out[m * N + n] = squareplus(ste_clamp(o, -50.0f, 50.0f));
+        }
+    }
+}
+
 /* Plain int32 GEMM C[m,n] = sum_k A[m,k] W[n,k] (the bare BitLinear contraction). */
 void orc_gemm_i8_i32(const int8_t* A, const int8_t* W, int32_t* C, int64_t M, int64_t N, int64_t K,
                      int nthreads) {

@@ -209,6 +209,22 @@ def test_quantize_rows_narrow_strided(cuda_dev, K):
     _eq(s[~np.isnan(s)], s_ref[~np.isnan(s_ref)], "xscale")
 
 
+@pytest.mark.parametrize("K", [48, 200])
+def test_quantize_rows_clears_the_given_rows(cuda_dev, K):
+    # the dt quantisation zero-fills the fused scan's row-maximum array on the way,
+    # without changing its own outputs (narrow and wide rows)
+    k = _mi()
+    g = np.random.default_rng(3 + K)
+    x = g.standard_normal((257, K)).astype(np.float32)
+    q_ref, s_ref = orc.quant_rows(x)
+    xd = torch.from_numpy(x).to(cuda_dev)
+    clear = torch.full((257,), 5.0, device=cuda_dev)
+    q, s = k.quantize_rows(xd, clear=clear)
+    _eq(q, q_ref, "xq")
+    _eq(s, s_ref, "xscale")
+    assert torch.equal(clear, torch.zeros_like(clear))
+
+
 @pytest.mark.parametrize("D", [256, 768])
 def test_rowprep_fused_matches_oracle(cuda_dev, D):
     k = _mi()
