@@ -26,7 +26,7 @@ rank 0 only, a bounded sample of the same workload per step.
 
 --profile-workload runs one kernel class of a benchmark configuration a few
 times on cuda:0 with the seeded inputs (for ncu captures; nothing is timed):
-config2, config3, config3-packed, config4-in_proj, config5-step.
+config2, config3, config3-packed, config3-norm-sqp, config4-in_proj, config5-step.
 """
 from __future__ import annotations
 
@@ -504,6 +504,18 @@ def _pw_config3(dev, launches: int, packed: bool) -> None:
             kernels.bitlinear_i8(A, Wq, out=C)
 
 
+def _pw_config3_norm_sqp(dev, launches: int) -> None:
+    from mamba_integer_b200 import kernels, synth
+
+    A, a_scale, Wq, ws = synth.bitlinear_inputs()
+    gamma, step = (t.to(dev) for t in synth.bitlinear_norm_params(Wq.shape[0]))
+    A, Wq, a_scale = A.to(dev), Wq.to(dev), a_scale.to(dev)
+    Wp = kernels.pack_ternary(Wq)
+    w_sc = torch.tensor([ws], dtype=torch.float32, device=dev)
+    for _ in range(launches):
+        kernels.bitlinear_packed_norm_sqp(A, Wp, a_scale, w_sc, gamma, step)
+
+
 def _pw_config4_in_proj(dev, launches: int) -> None:
     """One layer's in_proj of the config-4 prefill at full size: int8 A
     [131072, 768] x packed ternary W [3072, 768] -> fp32 [131072, 3072] with
@@ -545,6 +557,7 @@ PROFILE_WORKLOADS = {
     "config2": lambda dev, k: _pw_config2(dev, k),
     "config3": lambda dev, k: _pw_config3(dev, k, packed=False),
     "config3-packed": lambda dev, k: _pw_config3(dev, k, packed=True),
+    "config3-norm-sqp": lambda dev, k: _pw_config3_norm_sqp(dev, k),
     "config4-in_proj": lambda dev, k: _pw_config4_in_proj(dev, k),
     "config5-step": lambda dev, k: _pw_config5_step(dev, k),
 }

@@ -312,6 +312,27 @@ int mi_argmax_rows(const float* x, int ldx, int T, int V, int64_t* out, void* st
  * Replaces: dyadic_scan_triton_fast(u, nums), src/triton_kernels/dyadic_scan.py:462. */
 int mi_scan_convex(const float* u, const float* nums, float* h, int batch, int L, int DN, void* stream);
 
+/*
+ * Training side.  Backward of the convex dyadic scan: grad_h, h (the forward's
+ * output), u, nums [batch, L, DN] fp32 -> grad_u, grad_nums (same shape):
+ *   g[t] = grad_h[t] + (nums[t]/32768) * g[t+1];  grad_u = (1 - nums/32768) * g;
+ *   grad_nums[t] = (g[t] * (h[t-1] - u[t])) / 32768  (h[-1] = 0).
+ * Replaces: dyadic_scan_backward_triton_fast, src/triton_kernels/dyadic_scan.py:376-459
+ * (DyadicScanFunction.backward, src/mamba_integer_model.py:316-344).
+ */
+int mi_scan_convex_backward(const float* grad_h, const float* h, const float* u, const float* nums,
+                            float* grad_u, float* grad_nums, int batch, int L, int DN, void* stream);
+
+/*
+ * Training side.  Straight-through backward of the per-token int8 activation
+ * quantisation: grad_xq [T, K], amax [T] (each row's max |x|, the scale the
+ * forward saved) -> grad_x [T, K] =
+ *   clamp((grad_xq * 127) / clamp(amax, min=0.01), -100, 100).
+ * With K % 4 == 0, grad_xq and grad_x must be 16-byte aligned.
+ * Replaces: QuantizeActivationsFunction.backward, src/triton_kernels/bitnet_kernels.py:77-95.
+ */
+int mi_quant_ste_backward(const float* grad_xq, const float* amax, float* grad_x, int T, int K, void* stream);
+
 /* Element-wise ops (n elements, contiguous).
  * Replace fused_squareplus_clamp / fused_ste_clamp / fused_sigmoid_gate,
  * src/triton_kernels/fused_activations.py:229, :511, :399. */

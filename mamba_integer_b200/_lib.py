@@ -35,6 +35,8 @@ SIGNATURES = {
     "mi_bitlinear_i8": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
     "mi_pack_ternary": [_p, _i, _p, _i, _i, _p],
     "mi_bitlinear_packed": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p],
+    "mi_scan_convex_backward": [_p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
+    "mi_quant_ste_backward": [_p, _p, _p, _i, _i, _p],
     "mi_bitlinear_packed_norm_sqp": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _p, _i, _p, _i, _i, _i, _p],
     "mi_conv_act_quant": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_conv_act_quant_noalloc": [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],

@@ -7,4 +7,5 @@
 #include "ssm.cu"
 #include "gemm_i8.cu"
 #include "decode.cu"
+#include "train.cu"
 #include "noalloc.cu"

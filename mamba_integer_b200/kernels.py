@@ -385,7 +385,67 @@ def fast_bitshift_norm(x, gamma, step_size=None):
     return bitshift_norm(x.contiguous(), gamma, step)
 
 
-fast_quantize_activations = quantize_activations
+def scan_convex_backward(grad_h: torch.Tensor, h: torch.Tensor, u: torch.Tensor, nums: torch.Tensor
+                         ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Backward of the convex dyadic scan (mi_scan_convex_backward): (grad_u, grad_nums)."""
+    for t, nm in ((grad_h, "grad_h"), (h, "h"), (u, "u"), (nums, "nums")):
+        _need(t, torch.float32, nm)
+        if t.shape != grad_h.shape or t.dim() != 3:
+            raise ValueError(f"{nm} must be [batch, L, DN] like grad_h")
+    B, L, DN = grad_h.shape
+    gu = torch.empty_like(grad_h)
+    gn = torch.empty_like(grad_h)
+    _lib.check(_lib.load().mi_scan_convex_backward(grad_h.data_ptr(), h.data_ptr(), u.data_ptr(), nums.data_ptr(),
+                                                   gu.data_ptr(), gn.data_ptr(), B, L, DN, _stream()),
+               "mi_scan_convex_backward")
+    return gu, gn
+
+
+def quant_ste_backward(grad_xq: torch.Tensor, amax: torch.Tensor) -> torch.Tensor:
+    """Straight-through backward of the activation quantisation (mi_quant_ste_backward):
+    grad_xq [T, K], amax [T] (each row's max |x|) -> grad_x [T, K]."""
+    _need(grad_xq, torch.float32, "grad_xq")
+    _need(amax, torch.float32, "amax")
+    T, K = grad_xq.shape
+    if amax.numel() != T:
+        raise ValueError("amax must hold one value per row")
+    gx = torch.empty_like(grad_xq)
+    _lib.check(_lib.load().mi_quant_ste_backward(grad_xq.data_ptr(), amax.data_ptr(), gx.data_ptr(), T, K, _stream()),
+               "mi_quant_ste_backward")
+    return gx
+
+
+class QuantizeActivationsFunction(torch.autograd.Function):
+    """Activation quantisation with the reference's straight-through backward
+    (src/triton_kernels/bitnet_kernels.py:48-95): forward (xq as fp32 integer
+    values, amax / 127); backward clamp(grad * 127 / clamp(amax, min=0.01), +-100)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        K = x.shape[-1]
+        x2 = x.detach().float().contiguous().view(-1, K)
+        # the row maximum the backward needs (the reference saves max(amax, 1e-8) itself,
+        # which amax / 127 does not give back exactly); a maximum is exact in any order
+        amax = x2.abs().amax(-1).clamp(min=1e-8).contiguous()
+        q, s = quantize_rows(x2, amax=amax)
+        ctx.save_for_backward(amax)
+        ctx.original_shape = x.shape
+        return q.to(torch.float32).view(x.shape), s.view(*x.shape[:-1], 1)
+
+    @staticmethod
+    def backward(ctx, grad_x_quant, grad_scale):
+        (amax,) = ctx.saved_tensors
+        K = ctx.original_shape[-1]
+        g = grad_x_quant.float().contiguous().view(-1, K)
+        return quant_ste_backward(g, amax).view(ctx.original_shape)
+
+
+def fast_quantize_activations(x):
+    """Triton-name wrapper of the reference (src/triton_kernels/bitnet_kernels.py:98):
+    quantisation with the straight-through backward."""
+    return QuantizeActivationsFunction.apply(x)
+
+
 fused_squareplus_clamp = squareplus_clamp
 fused_ste_clamp = ste_clamp
 fused_sigmoid_gate = sigmoid_gate

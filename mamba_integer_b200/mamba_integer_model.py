@@ -41,18 +41,25 @@ class BitShiftNormFunction(torch.autograd.Function):
 
 
 class DyadicScanFunction(torch.autograd.Function):
-    """Forward of src/mamba_integer_model.py:271-315 (convex combination scan,
-    decay = nums / 2^15)."""
+    """src/mamba_integer_model.py:260-366 (convex combination scan, decay = nums / 2^15):
+    forward on mi_scan_convex, backward on mi_scan_convex_backward (the quantities of
+    the reference's fast backward, src/triton_kernels/dyadic_scan.py:376-459)."""
 
     @staticmethod
     def forward(ctx, u, decay_nums, decay_shifts):
         if not bool((decay_shifts == 15).all()):
             raise ValueError("this build supports decay_shifts == 15 only (the reference fast path)")
-        return kernels.scan_convex(u.contiguous().float(), decay_nums.contiguous().float())
+        u32 = u.detach().contiguous().float()
+        n32 = decay_nums.detach().contiguous().float()
+        h = kernels.scan_convex(u32, n32)
+        ctx.save_for_backward(u32, h, n32)
+        return h
 
     @staticmethod
-    def backward(ctx, grad_h):  # pragma: no cover - inference build
-        raise NotImplementedError("training-side kernels are not part of this build")
+    def backward(ctx, grad_h):
+        u, h, nums = ctx.saved_tensors
+        grad_u, grad_nums = kernels.scan_convex_backward(grad_h.contiguous().float(), h, u, nums)
+        return grad_u, grad_nums, None
 
 
 class BitShiftNorm(nn.Module):

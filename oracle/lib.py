@@ -54,6 +54,11 @@ def _load():
     lib.orc_pack_ternary.argtypes = [_i8p, _i64, _i64, _u8p]
     lib.orc_unpack_ternary.restype = None
     lib.orc_unpack_ternary.argtypes = [_u8p, _i64, _i64, _i8p]
+    lib.orc_scan_convex_backward.restype = None
+    lib.orc_scan_convex_backward.argtypes = [_f32p, _f32p, _f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64,
+                                             ctypes.c_int]
+    lib.orc_quant_ste_backward.restype = None
+    lib.orc_quant_ste_backward.argtypes = [_f32p, _f32p, _f32p, _i64, _i64]
     lib.orc_bitlinear_norm_sqp.restype = None
     lib.orc_bitlinear_norm_sqp.argtypes = [_i32p, _f32p, ctypes.c_float, _f32p, ctypes.c_float, _f32p, _i64p, _i64,
                                            _i64, ctypes.c_int]
@@ -169,6 +174,27 @@ def gemm_i8_i32(A, W, nthreads=0):
     C = np.empty((M, N), np.int32)
     _load().orc_gemm_i8_i32(_p(A, _i8p), _p(W, _i8p), _p(C, _i32p), M, N, K, nthreads)
     return C
+
+
+def scan_convex_backward(grad_h, h, u, nums, nthreads=0):
+    """Training-side convex scan backward: (grad_u, grad_nums), each [B, L, DN] fp32."""
+    grad_h, h, u, nums = (_c(a, np.float32) for a in (grad_h, h, u, nums))
+    Bsz, L, DN = grad_h.shape
+    gu = np.empty_like(grad_h)
+    gn = np.empty_like(grad_h)
+    _load().orc_scan_convex_backward(_p(grad_h, _f32p), _p(h, _f32p), _p(u, _f32p), _p(nums, _f32p), _p(gu, _f32p),
+                                     _p(gn, _f32p), Bsz, L, DN, nthreads)
+    return gu, gn
+
+
+def quant_ste_backward(grad_xq, amax):
+    """Training-side STE backward of the activation quantisation: grad_x [T, K]."""
+    grad_xq = _c(grad_xq, np.float32)
+    amax = _c(amax, np.float32)
+    T, K = grad_xq.shape
+    gx = np.empty_like(grad_xq)
+    _load().orc_quant_ste_backward(_p(grad_xq, _f32p), _p(amax, _f32p), _p(gx, _f32p), T, K)
+    return gx
 
 
 def bitlinear_norm_sqp(acc, a_scale, w_scale, gamma, step, nthreads=0):

@@ -478,6 +478,53 @@ void orc_scan_convex(const float* u, const float* nums, float* h, int64_t Bsz, i
 }
 
 /*
+ * Backward of the convex dyadic scan (training side), sequential in t from
+ * the end: the reference's DyadicScanFunction.backward branch at
+ * src/mamba_integer_model.py:319-344, which computes the same quantities as
+ * its Triton fast backward (src/triton_kernels/dyadic_scan.py:376-459):
+ *   g[t] = grad_h[t] + decay[t] * g[t+1]   (decay = nums / 32768)
+ *   grad_u[t] = (1 - decay[t]) * g[t]
+ *   grad_nums[t] = (g[t] * (h[t-1] - u[t])) / 32768      (h[-1] = 0)
+ * fp32, each operation rounded once, in that order.
+ */
+void orc_scan_convex_backward(const float* grad_h, const float* h, const float* u, const float* nums,
+                              float* grad_u, float* grad_nums, int64_t Bsz, int64_t L, int64_t DN, int nthreads) {
+#pragma omp parallel for collapse(2) schedule(static) ORC_THREADS(nthreads)
+    for (int64_t b = 0; b < Bsz; b++)
+        for (int64_t c = 0; c < DN; c++) {
+            float acc = 0.0f;
+            for (int64_t t = L - 1; t >= 0; t--) {
+                const int64_t o = (b * L + t) * DN + c;
+                const float d = nums[o] / 32768.0f;
+                const float da = d * acc;
+                acc = grad_h[o] + da;
+                const float iw = 1.0f - d;
+                grad_u[o] = iw * acc;
+                const float hp = t > 0 ? h[o - DN] : 0.0f;
+                const float diff = hp - u[o];
+                const float gd = acc * diff;
+                grad_nums[o] = gd / 32768.0f;
+            }
+        }
+}
+
+/*
+ * Straight-through backward of the activation quantisation (training side),
+ * src/triton_kernels/bitnet_kernels.py:77-95: per row with saved scale
+ * amax[t] (the row's max |x|),
+ *   grad_x = clamp((grad_xq * 127) / clamp(amax, min=0.01), -100, 100).
+ */
+void orc_quant_ste_backward(const float* grad_xq, const float* amax, float* grad_x, int64_t T, int64_t K) {
+    for (int64_t t = 0; t < T; t++) {
+        const float s = amax[t] != amax[t] ? amax[t] : (amax[t] < 0.01f ? 0.01f : amax[t]);
+        for (int64_t k = 0; k < K; k++) {
+            const float g = grad_xq[t * K + k] * 127.0f;
+            grad_x[t * K + k] = clamp_t(g / s, -100.0f, 100.0f);
+        }
+    }
+}
+
+/*
  * The selective-scan section of MambaIntegerBlock.forward
  * (src/mamba_integer_model.py:419-444) from the dt_proj output onward:
  *   mod  = ste_clamp(dt_proj_out, -20, 20)                        (:422)

@@ -79,3 +79,24 @@ def test_model_forward_matches_reference(name):
     assert list(logits.shape) == fx["logits_shape"]
     assert sha(logits) == fx["logits_sha256"]
     del L
+
+
+def test_backward_restatements_match_reference_golden():
+    # tests/golden/backward.npz: the reference's own DyadicScanFunction.backward
+    # (src/mamba_integer_model.py:319-344) and QuantizeActivationsFunction.backward
+    # (src/triton_kernels/bitnet_kernels.py:77-95), run by make_backward_golden.py
+    import os
+
+    import numpy as np
+
+    from oracle import lib
+
+    z = np.load(os.path.join(os.path.dirname(__file__), "golden", "backward.npz"))
+    for c in ("scan_a", "scan_b"):
+        assert np.array_equal(lib.scan_convex(z[c + ".u"], z[c + ".nums"]).view(np.uint32), z[c + ".h"].view(np.uint32))
+        gu, gn = lib.scan_convex_backward(z[c + ".grad_h"], z[c + ".h"], z[c + ".u"], z[c + ".nums"])
+        assert np.array_equal(gu.view(np.uint32), z[c + ".grad_u"].view(np.uint32)), c
+        assert np.array_equal(gn.view(np.uint32), z[c + ".grad_nums"].view(np.uint32)), c
+    for c in ("ste_a", "ste_b"):
+        gx = lib.quant_ste_backward(z[c + ".grad_xq"], z[c + ".amax"])
+        assert np.array_equal(gx.view(np.uint32), z[c + ".grad_x"].view(np.uint32)), c
