@@ -39,7 +39,23 @@ def needs_build() -> bool:
     return any(os.path.getmtime(s) > t for s in deps)
 
 
+BPE_SO = os.path.join(HERE, "libmi_bpe.so")
+BPE_SRC = os.path.join(HERE, "tokenizer", "bpe.cpp")
+
+
+def build_bpe(force: bool = False) -> str:
+    """The host-side tokenizer library libmi_bpe.so (g++, C++17)."""
+    deps = [BPE_SRC, os.path.join(HERE, "tokenizer", "unicode_classes.h"), os.path.join(ROOT, "include", "mi_bpe.h")]
+    if not force and os.path.exists(BPE_SO) and all(os.path.getmtime(d) <= os.path.getmtime(BPE_SO) for d in deps):
+        return BPE_SO
+    cxx = shutil.which("g++") or "g++"
+    subprocess.run([cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-o", BPE_SO + ".tmp", BPE_SRC], check=True)
+    os.replace(BPE_SO + ".tmp", BPE_SO)
+    return BPE_SO
+
+
 def build(verbose: bool = False, force: bool = False) -> str:
+    build_bpe(force=force)
     if not force and not needs_build():
         return SO
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"

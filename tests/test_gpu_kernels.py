@@ -430,8 +430,8 @@ def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split):
     ws = np.float32(2.0 ** -5)
     dtq, dts = orc.quant_rows(np.ascontiguousarray(xp[:, :R].numpy()))
     modraw = orc.bitlinear(dtq, dts, wdt.numpy(), ws)
-    y_ref = orc.ssm(act.numpy(), np.ascontiguousarray(xp[:, R:].numpy()), modraw,
-                    np.ascontiguousarray(z[:, D:].numpy()), base.numpy(), bsz, L)
+    y_ref, h_ref = orc.ssm(act.numpy(), np.ascontiguousarray(xp[:, R:].numpy()), modraw,
+                           np.ascontiguousarray(z[:, D:].numpy()), base.numpy(), bsz, L, want_h=True)
     dv = lambda t: t.to(cuda_dev)  # noqa: E731
     dtq_d = torch.zeros(T, R16, dtype=torch.int8, device=cuda_dev)
     dts_d = torch.empty(T, device=cuda_dev)
@@ -440,10 +440,12 @@ def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split):
     w16 = torch.zeros(D, R16, dtype=torch.int8)
     w16[:, :R] = wdt
     amax = torch.zeros(T, device=cuda_dev)
+    h_out = torch.full((bsz, D, 16), 7.0, device=cuda_dev)
     y = k.ssm_scan_dt(dv(act), xpd[:, R:], dtq_d, dts_d, dv(w16), dv(torch.tensor([ws])), R, zd[:, D:], dv(base),
-                      bsz, L, amax=amax, split=split)
+                      bsz, L, amax=amax, split=split, h_out=h_out)
     _eq(y, y_ref, "fused-dt ssm y")
     _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
+    _eq(h_out, h_ref, "final states")
 
 
 def test_scan_convex_and_elementwise_match_reference_fixtures(cuda_dev):
