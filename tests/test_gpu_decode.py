@@ -134,3 +134,43 @@ def test_argmax_rows_ties_nan_and_inf(cuda_dev):
     got = kernels.argmax_rows(x.to(cuda_dev)).cpu()
     assert got.tolist() == torch.argmax(x, dim=-1).tolist() == [17, 0, 5, 999, 0, got[5].item()]
     assert got[5].item() == int(torch.argmax(x[5]))
+
+
+@pytest.mark.parametrize("D,R", [(80, 16), (256, 16), (2048, 64)])
+def test_decode_mid_equals_unfused_step_kernels(cuda_dev, D, R):
+    # mi_decode_mid (one CTA per stream for D % 64 != 0, a 4-CTA cluster per stream otherwise)
+    # against conv step -> x_proj GEMM -> scan step, each of which is checked against the oracle
+    from mamba_integer_b200 import kernels as k
+    g = torch.Generator().manual_seed(D + R)
+    B, N, P = 37, 16, R + 32
+    R16 = (R + 15) // 16 * 16
+    dv = lambda t: t.to(cuda_dev)  # noqa: E731
+    xz = dv(torch.randn(B, 2 * D, generator=g) * 2)
+    cw = dv((torch.rand(D, 4, generator=g) - 0.5).contiguous())
+    cb = dv(torch.rand(D, generator=g) - 0.5)
+    win0 = torch.randn(B, 3, D, generator=g)
+    w_x = dv(torch.randint(-1, 2, (P, D), generator=g, dtype=torch.int8))
+    w_x_scale = dv(torch.tensor([2.0 ** -6]))
+    w_dt = torch.zeros(D, R16, dtype=torch.int8)
+    w_dt[:, :R] = torch.randint(-1, 2, (D, R), generator=g, dtype=torch.int8)
+    w_dt, w_dt_scale = dv(w_dt), dv(torch.tensor([2.0 ** -5]))
+    base = dv(torch.randint(29492, 32736, (D, N), generator=g).float())
+    h0 = torch.randn(B, D, N, generator=g)
+    # unfused
+    win1, h1 = dv(win0.clone()), dv(h0.clone())
+    act = torch.empty(B, D, device=cuda_dev)
+    xq1, xs1 = torch.empty(B, D, dtype=torch.int8, device=cuda_dev), torch.empty(B, device=cuda_dev)
+    k.conv_step(xz, cw, cb, win1, D, xq1, xs1, act=act)
+    xp = k.bitlinear_i8(xq1, w_x, xs1, w_x_scale)
+    yq1, ys1 = torch.empty(B, D, dtype=torch.int8, device=cuda_dev), torch.empty(B, device=cuda_dev)
+    k.ssm_step(act, xp, R, w_dt, w_dt_scale, xz[:, D:], base, h1, yq1, ys1)
+    # fused
+    win2, h2 = dv(win0.clone()), dv(h0.clone())
+    yq2, ys2 = torch.empty(B, D, dtype=torch.int8, device=cuda_dev), torch.empty(B, device=cuda_dev)
+    xp2 = torch.empty(B, P, device=cuda_dev)
+    k.decode_mid(xz, cw, cb, win2, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h2, yq2, ys2, xp_out=xp2)
+    assert torch.equal(win1, win2)
+    assert torch.equal(xp.view(torch.int32), xp2.view(torch.int32))
+    assert torch.equal(h1.view(torch.int32), h2.view(torch.int32))
+    assert torch.equal(yq1, yq2)
+    assert torch.equal(ys1.view(torch.int32), ys2.view(torch.int32))
