@@ -167,12 +167,20 @@ __device__ __forceinline__ float ssm_channel_step(int c, float actv, float zv, c
     const float xdt = __fmul_rn(actv, dtv);
     float4* hp = reinterpret_cast<float4*>(hrow);
     const float4* bp = reinterpret_cast<const float4*>(base + (size_t)c * NS);
+    // all 16 states and bases are loaded before the first store: the stores go
+    // through the same row pointer, so a load placed after one could not be
+    // issued before it, and the four 16-byte pieces would cost four round trips
+    float4 hv4[NS / 4], bv4[NS / 4];
+#pragma unroll
+    for (int q = 0; q < NS / 4; q++) {
+        hv4[q] = hp[q];
+        bv4[q] = bp[q];
+    }
     float yacc = 0.0f;
 #pragma unroll
     for (int q = 0; q < NS / 4; q++) {
-        const float4 hv4 = hp[q], bv4 = bp[q];
-        float hv[4] = {hv4.x, hv4.y, hv4.z, hv4.w};
-        const float bv[4] = {bv4.x, bv4.y, bv4.z, bv4.w};
+        float hv[4] = {hv4[q].x, hv4[q].y, hv4[q].z, hv4[q].w};
+        const float bv[4] = {bv4[q].x, bv4[q].y, bv4[q].z, bv4[q].w};
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int n = 4 * q + e;
@@ -183,8 +191,10 @@ __device__ __forceinline__ float ssm_channel_step(int c, float actv, float zv, c
             hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));  // (:309)
             yacc = __fmaf_rn(hv[e], bc[NS + n], yacc);                                 // (:440)
         }
-        hp[q] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        hv4[q] = make_float4(hv[0], hv[1], hv[2], hv[3]);
     }
+#pragma unroll
+    for (int q = 0; q < NS / 4; q++) hp[q] = hv4[q];
     return sigmoid_gate(yacc, zv);                                                      // (:441-444)
 }
 
