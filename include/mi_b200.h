@@ -300,6 +300,19 @@ int mi_decode_mid(const float* xz, int ldx, const float* conv_w, const float* co
                   float* xscale, int batch, int D, int N, void* stream);
 
 /*
+ * mi_decode_mid_packed: mi_decode_mid with the x_proj weights in the 2-bit
+ * packed form of mi_pack_ternary (w_x_packed uint8 [R + 2N, D/4], 4-byte
+ * aligned), which every stream reads a quarter as many bytes of.  Same
+ * results bit for bit.  D % 64 == 0 (a cluster of 4 CTAs per stream, each a
+ * slice of whole 16-weight words), D <= 4096, R <= 64, N == 16.
+ * Replaces: as mi_decode_mid, src/mamba_integer_model.py:404-444.
+ */
+int mi_decode_mid_packed(const float* xz, int ldx, const float* conv_w, const float* conv_b, float* win,
+                         const uint8_t* w_x_packed, const float* w_x_scale, int R, const int8_t* w_dt,
+                         const float* w_dt_scale, const float* base, float* h, float* xp_out, int8_t* xq,
+                         float* xscale, int batch, int D, int N, void* stream);
+
+/*
  * mi_argmax_rows: out[t] = torch.argmax(x[t, :V]) (first index of the
  * maximum; NaN counts as the maximum), x rows of stride ldx.
  * Replaces the greedy choice over logits[:, -1, :] in the generation loop,

@@ -46,6 +46,7 @@ SIGNATURES = {
     "mi_conv_step": [_p, _i, _p, _p, _p, _p, _p, _p, _i, _i, _p],
     "mi_ssm_step": [_p, _p, _i, _i, _p, _p, _p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_decode_mid": [_p, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
+    "mi_decode_mid_packed": [_p, _i, _p, _p, _p, _p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p],
     "mi_argmax_rows": [_p, _i, _i, _i, _p, _p],
     "mi_scan_convex": [_p, _p, _p, _i, _i, _i, _p],
     "mi_squareplus_clamp": [_p, _p, _i64, _f, _f, _p],

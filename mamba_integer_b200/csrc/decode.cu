@@ -385,12 +385,68 @@ decode_mid_kernel(const float* __restrict__ xz, int ldx, const float* __restrict
 // 1.62 for 4 x 64, 1.73 for 4 x 256, 1.78 for 8 x 128
 constexpr int MC_CS = 4;          // CTAs per stream (a portable cluster size)
 constexpr int MC_THREADS = 128;
-constexpr int MC_XO = 4;          // x_proj outputs per warp pass
+constexpr int MC_XO = 4;          // x_proj outputs per warp pass (int8 weights)
+constexpr int MC_XOP = 12;        // x_proj outputs per warp pass (2-bit packed weights)
 constexpr int MC_MAX_DC = MAX_D / MC_CS;
+// at most 64 registers a thread: 8 CTAs per SM, so 256 streams (1024 CTAs) are one wave
+constexpr int MC_MIN_CTAS = 8;
 
-__global__ void __cluster_dims__(MC_CS, 1, 1) __launch_bounds__(MC_THREADS)
+// One channel of the scan step with its 16 states already in registers (hv4,
+// updated in place; the caller stores them): dt_proj, decay / dt / u, the
+// convex update, y = sum h*C and the gate, in ssm_channel_step's order.
+__device__ __forceinline__ float ssm_channel_update(int c, float actv, float zv, const int32_t* dtq, int R16,
+                                                    const int8_t* __restrict__ w_dt, float dscale,
+                                                    const float* __restrict__ base, float4 (&hv4)[4],
+                                                    const float* bc) {
+    constexpr int NS = 16;
+    const int4* wq = reinterpret_cast<const int4*>(w_dt + (size_t)c * R16);
+    const float4* bp = reinterpret_cast<const float4*>(base + (size_t)c * NS);
+    // the dt_proj row and the bases are loaded together (R16 <= 64: at most 4 chunks)
+    int4 wv[MAX_R16 / 16];
+#pragma unroll
+    for (int k = 0; k < MAX_R16 / 16; k++) wv[k] = k < R16 / 16 ? wq[k] : make_int4(0, 0, 0, 0);
+    float4 bv4[NS / 4];
+#pragma unroll
+    for (int q = 0; q < NS / 4; q++) bv4[q] = bp[q];
+    int acc = 0;
+#pragma unroll
+    for (int k = 0; k < MAX_R16 / 16; k++) {
+        if (k < R16 / 16) {
+            acc = __dp4a(dtq[4 * k], wv[k].x, acc);
+            acc = __dp4a(dtq[4 * k + 1], wv[k].y, acc);
+            acc = __dp4a(dtq[4 * k + 2], wv[k].z, acc);
+            acc = __dp4a(dtq[4 * k + 3], wv[k].w, acc);
+        }
+    }
+    const float mod = ste_clamp(__fmul_rn((float)acc, dscale), -20.0f, 20.0f);                   // (:419-421)
+    const float dtv = ste_clamp(__fmul_rn(squareplus_bounded(mod), 0.01f), 0.001f, 0.1f);          // (:425-427)
+    const float xdt = __fmul_rn(actv, dtv);
+    float yacc = 0.0f;
+#pragma unroll
+    for (int q = 0; q < NS / 4; q++) {
+        float hv[4] = {hv4[q].x, hv4[q].y, hv4[q].z, hv4[q].w};
+        const float bv[4] = {bv4[q].x, bv4[q].y, bv4[q].z, bv4[q].w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int n = 4 * q + e;
+            const float num = ste_clamp(__fadd_rn(bv[e], mod), 0.0f, 32000.0f);                // (:423-424, :305)
+            const float dec = __fmul_rn(num, 3.0517578125e-05f);
+            const float u = __fmul_rn(xdt, bc[n]);
+            hv[e] = __fadd_rn(__fmul_rn(hv[e], dec), __fmul_rn(__fsub_rn(1.0f, dec), u));  // (:309)
+            yacc = __fmaf_rn(hv[e], bc[NS + n], yacc);                                 // (:440)
+        }
+        hv4[q] = make_float4(hv[0], hv[1], hv[2], hv[3]);
+    }
+    return sigmoid_gate(yacc, zv);                                                      // (:441-444)
+}
+
+// PACKED_X: w_x is the 2-bit packed form [R + 2N, D/4] (pack_ternary's layout)
+// instead of int8 [R + 2N, D]; a quarter of the bytes for every stream's CTAs
+// to read, and each lane loads its weight words for MC_XOP outputs at once.
+template <bool PACKED_X>
+__global__ void __cluster_dims__(MC_CS, 1, 1) __launch_bounds__(MC_THREADS, MC_MIN_CTAS)
 decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ cw,
-                          const float* __restrict__ cb, float* __restrict__ win, const int8_t* __restrict__ w_x,
+                          const float* __restrict__ cb, float* __restrict__ win, const void* __restrict__ w_x_any,
                           const float* __restrict__ w_x_scale, int R, const int8_t* __restrict__ w_dt,
                           const float* __restrict__ w_dt_scale, const float* __restrict__ base,
                           float* __restrict__ h, float* __restrict__ xp_out, int8_t* __restrict__ xq,
@@ -416,6 +472,8 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     const int c0 = rank * DC;
     const float* xrow = xz + (size_t)b * ldx;
     float* wrow = win + (size_t)b * 3 * D;
+    float* hbase = h + ((size_t)b * D + c0) * NS;  // this CTA's state rows
+    const float wxs = *w_x_scale, wdts = *w_dt_scale;
 
     // (1) conv + activation of this CTA's channels, into shared memory
     unsigned m = 0u;
@@ -437,40 +495,76 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
         *reinterpret_cast<char4*>(xq_s + 4 * i) = quant4(*reinterpret_cast<const float4*>(act_s + 4 * i), inv_c);
     __syncthreads();
     // (3) x_proj: exact int32 partial dot products over this CTA's channels, summed across the
-    // cluster.  A warp takes MC_XO outputs at a time with all their weight loads issued first.
+    // cluster.  A warp takes a group of outputs at a time with all their weight loads issued first.
     const int nch = DC / 16;
-    for (int o0 = warp * MC_XO; o0 < P; o0 += NW * MC_XO) {
-        int acc[MC_XO];
+    if (PACKED_X) {
+        // one 32-bit word = 16 ternary weights = one 16-byte chunk of the int8 row
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(w_x_any) + c0 / 16;
+        const int wpitch = D / 16;
+        for (int o0 = warp * MC_XOP; o0 < P; o0 += NW * MC_XOP) {
+            int acc[MC_XOP];
 #pragma unroll
-        for (int u = 0; u < MC_XO; u++) acc[u] = 0;
-        for (int j = lane; j < nch; j += 32) {
-            const int4 xv = reinterpret_cast<const int4*>(xq_s)[j];
-            int4 wv[MC_XO];
+            for (int u = 0; u < MC_XOP; u++) acc[u] = 0;
+            for (int j = lane; j < nch; j += 32) {
+                uint32_t wv[MC_XOP];
 #pragma unroll
-            for (int u = 0; u < MC_XO; u++)
-                wv[u] = o0 + u < P ? reinterpret_cast<const int4*>(w_x + (size_t)(o0 + u) * D + c0)[j]
-                                   : make_int4(0, 0, 0, 0);
+                for (int u = 0; u < MC_XOP; u++) wv[u] = o0 + u < P ? wp[(size_t)(o0 + u) * wpitch + j] : 0u;
+                const int4 xv = reinterpret_cast<const int4*>(xq_s)[j];
 #pragma unroll
-            for (int u = 0; u < MC_XO; u++) {
-                acc[u] = __dp4a(xv.x, wv[u].x, acc[u]);
-                acc[u] = __dp4a(xv.y, wv[u].y, acc[u]);
-                acc[u] = __dp4a(xv.z, wv[u].z, acc[u]);
-                acc[u] = __dp4a(xv.w, wv[u].w, acc[u]);
+                for (int u = 0; u < MC_XOP; u++) {
+                    const uint4 w16 = mi::gemm::unpack16(wv[u]);
+                    acc[u] = __dp4a(xv.x, (int)w16.x, acc[u]);
+                    acc[u] = __dp4a(xv.y, (int)w16.y, acc[u]);
+                    acc[u] = __dp4a(xv.z, (int)w16.z, acc[u]);
+                    acc[u] = __dp4a(xv.w, (int)w16.w, acc[u]);
+                }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+                for (int u = 0; u < MC_XOP; u++) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int u = 0; u < MC_XOP; u++)
+                    if (o0 + u < P) part_xp[o0 + u] = acc[u];
             }
         }
+    } else {
+        const int8_t* w_x = reinterpret_cast<const int8_t*>(w_x_any);
+        for (int o0 = warp * MC_XO; o0 < P; o0 += NW * MC_XO) {
+            int acc[MC_XO];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) {
+            for (int u = 0; u < MC_XO; u++) acc[u] = 0;
+            for (int j = lane; j < nch; j += 32) {
+                const int4 xv = reinterpret_cast<const int4*>(xq_s)[j];
+                int4 wv[MC_XO];
 #pragma unroll
-            for (int u = 0; u < MC_XO; u++) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
-        }
-        if (lane == 0) {
+                for (int u = 0; u < MC_XO; u++)
+                    wv[u] = o0 + u < P ? reinterpret_cast<const int4*>(w_x + (size_t)(o0 + u) * D + c0)[j]
+                                       : make_int4(0, 0, 0, 0);
 #pragma unroll
-            for (int u = 0; u < MC_XO; u++)
-                if (o0 + u < P) part_xp[o0 + u] = acc[u];
+                for (int u = 0; u < MC_XO; u++) {
+                    acc[u] = __dp4a(xv.x, wv[u].x, acc[u]);
+                    acc[u] = __dp4a(xv.y, wv[u].y, acc[u]);
+                    acc[u] = __dp4a(xv.z, wv[u].z, acc[u]);
+                    acc[u] = __dp4a(xv.w, wv[u].w, acc[u]);
+                }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+                for (int u = 0; u < MC_XO; u++) acc[u] += __shfl_xor_sync(0xffffffffu, acc[u], off);
+            }
+            if (lane == 0) {
+#pragma unroll
+                for (int u = 0; u < MC_XO; u++)
+                    if (o0 + u < P) part_xp[o0 + u] = acc[u];
+            }
         }
     }
     cluster.sync();
-    const float sc_x = __fmul_rn(*w_x_scale, xs_c);  // (w_scale * x_scale), as the GEMM epilogue
+    const float sc_x = __fmul_rn(wxs, xs_c);  // (w_scale * x_scale), as the GEMM epilogue
     for (int o = threadIdx.x; o < P; o += MC_THREADS) {
         int acc = 0;
 #pragma unroll
@@ -483,13 +577,20 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     // (4) the dt row's quantisation (every CTA of the cluster computes the same)
     if (warp == 0) dt_row_quant(xp_s, R, R16, dtq_s, &dts_s);
     __syncthreads();
-    const float dscale = __fmul_rn(*w_dt_scale, dts_s);
-    // (5) scan step + gate of this CTA's channels; y replaces act in shared memory
+    const float dscale = __fmul_rn(wdts, dts_s);
+    // (5) scan step + gate of this CTA's channels; y replaces act in shared memory.  (Staging
+    // the next channels' states in shared memory by cp.async was slower: the smem it takes
+    // comes out of the L1 that holds the weights every stream's CTAs read.)
     unsigned my = 0u;
     for (int i = threadIdx.x; i < DC; i += MC_THREADS) {
         const int c = c0 + i;
-        const float yv = ssm_channel_step(c, act_s[i], xrow[D + c], dtq_s, R16, w_dt, dscale, base,
-                                          h + ((size_t)b * D + c) * NS, xp_s + R);
+        float4* hp = reinterpret_cast<float4*>(hbase + (size_t)i * NS);
+        float4 hv4[NS / 4];
+#pragma unroll
+        for (int q = 0; q < NS / 4; q++) hv4[q] = hp[q];
+        const float yv = ssm_channel_update(c, act_s[i], xrow[D + c], dtq_s, R16, w_dt, dscale, base, hv4, xp_s + R);
+#pragma unroll
+        for (int q = 0; q < NS / 4; q++) hp[q] = hv4[q];
         act_s[i] = yv;
         my = max(my, __float_as_uint(fabsf(yv)));
     }
@@ -645,13 +746,37 @@ extern "C" int mi_decode_mid(const float* xz, int ldx, const float* conv_w, cons
     if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
     if (D % (16 * MC_CS) == 0 && (long long)batch * MC_CS <= 0x7fffffffLL) {
         // a cluster of MC_CS CTAs per stream (each channel slice a multiple of 16 bytes of int8)
-        decode_mid_cluster_kernel<<<batch * MC_CS, MC_THREADS, 0, (cudaStream_t)stream>>>(
+        decode_mid_cluster_kernel<false><<<batch * MC_CS, MC_THREADS, 0, (cudaStream_t)stream>>>(
             xz, ldx, conv_w, conv_b, win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
     } else {
         decode_mid_kernel<<<batch, MID_THREADS, 0, (cudaStream_t)stream>>>(xz, ldx, conv_w, conv_b, win, w_x,
                                                                             w_x_scale, R, w_dt, w_dt_scale, base, h,
                                                                             xp_out, xq, xscale, D);
     }
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
+extern "C" int mi_decode_mid_packed(const float* xz, int ldx, const float* conv_w, const float* conv_b, float* win,
+                                    const uint8_t* w_x_packed, const float* w_x_scale, int R, const int8_t* w_dt,
+                                    const float* w_dt_scale, const float* base, float* h, float* xp_out,
+                                    int8_t* xq, float* xscale, int batch, int D, int N, void* stream) {
+    using namespace mi::decode;
+    if (!xz || !conv_w || !conv_b || !win || !w_x_packed || !w_x_scale || !w_dt || !w_dt_scale || !base || !h ||
+        !xq || !xscale)
+        return MI_ERR_INVALID;
+    if (N != 16) return MI_ERR_UNSUPPORTED;
+    if (batch <= 0 || D <= 0 || R <= 0 || ldx < 2 * D) return MI_ERR_INVALID;
+    // each CTA's channel slice is a whole number of 16-weight words
+    if (D % (16 * MC_CS) != 0 || D > MAX_D || (R + 15) / 16 * 16 > MAX_R16 || ldx % 4 != 0)
+        return MI_ERR_UNSUPPORTED;
+    if ((long long)batch * MC_CS > 0x7fffffffLL) return MI_ERR_UNSUPPORTED;
+    if (((uintptr_t)xz | (uintptr_t)conv_w | (uintptr_t)conv_b | (uintptr_t)win | (uintptr_t)h | (uintptr_t)base |
+         (uintptr_t)w_dt) & 15)
+        return MI_ERR_INVALID;
+    if (((uintptr_t)w_x_packed | (uintptr_t)xq) & 3) return MI_ERR_INVALID;
+    decode_mid_cluster_kernel<true><<<batch * MC_CS, MC_THREADS, 0, (cudaStream_t)stream>>>(
+        xz, ldx, conv_w, conv_b, win, w_x_packed, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
     MI_CHECK_LAUNCH();
     return MI_OK;
 }

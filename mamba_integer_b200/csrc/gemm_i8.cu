@@ -24,6 +24,7 @@
 //
 // The accumulation is exact: |sum| <= 127*K < 2^31, and int -> fp32 is exact
 // below 2^24 (K <= 132104), the range every BitLinear of the model is in.
+#include <cstdlib>
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -852,6 +853,305 @@ static int sm_count() {
     return num_sms;
 }
 
+// ---------------------------------------------------------------------------
+// 2-SM variant (tcgen05.mma.cta_group::2): a cluster of two CTAs computes one
+// 256 x 256 output tile.  CTA rank r loads rows [m0 + 128r, +128) of A and the
+// 128-row half [n0 + 128r, +128) of the weights into its own shared memory;
+// the leader (rank 0) issues M=256, N=256 MMAs that read both CTAs' halves and
+// accumulate rows 128r.. into CTA r's TMEM.  Per SM this halves the weight
+// bytes staged and read per MMA, which is what bounds the one-CTA kernel
+// (its shared-memory traffic per K-slice exceeds the MMA time).
+// Synchronisation: the leader's full barrier counts both CTAs' TMA bytes
+// (each CTA's loads signal it through its cluster address); MMA completions
+// are committed to both CTAs' barriers (multicast commit); the epilogue warps
+// of both CTAs arrive on the leader's barrier remotely.  No TMA multicast:
+// each CTA loads its own operands.  All waits are bounded, and every path
+// reaches the final cluster barrier before TMEM is freed.
+// Int8 weights only: a packed-weight version (each CTA expanding its weight
+// half, the peer's readiness relayed to the leader) was correct but slower
+// than the one-CTA packed kernel at config 3 (0.38 vs 0.25 ms), so packed
+// weights keep the one-CTA kernels.
+// ---------------------------------------------------------------------------
+constexpr int BM2 = 256;   // M of the pair's MMA (128 rows per CTA)
+constexpr int BN2 = 256;   // N of the pair's MMA (128 weight rows per CTA)
+constexpr int HALF = 128;
+
+struct Cfg2 {
+    static constexpr int A_BYTES = HALF * BK;   // this CTA's A rows
+    static constexpr int B_BYTES = HALF * BK;   // this CTA's weight half
+    // six stages and one staging box per epilogue warp measured best at config 3
+    // (0.1885 ms, against 0.200 with five stages and two boxes)
+    static constexpr int STAGES = 6;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int TMEM_COLS = 256;       // per accumulator (N = 256)
+    static constexpr int EPI_BOXES = BN2 / 32;
+    static constexpr int STG_BUFS = 1;
+    static constexpr int STG_BYTES = EPI_WARPS * STG_BUFS * 4096;
+    static constexpr int BAR_BYTES = 256;
+    static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
+    static_assert(STAGE_BYTES % 1024 == 0, "1024-byte alignment of the swizzled tiles");
+    static_assert(8 * (2 * STAGES + 4) + 16 <= BAR_BYTES, "barrier block");
+    static_assert(SMEM <= 227 * 1024, "shared memory per CTA");
+};
+
+__host__ __device__ constexpr uint32_t idesc_i8_2sm() {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN2 >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// shared::cluster address of the same variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];\n" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on the pair leader's barrier
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* tm, uint32_t leader_bar, int x,
+                                                 int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+        "%4}], [%2];\n" ::"r"(dst),
+        "l"((uint64_t)tm), "r"(leader_bar), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void mma_i8_2sm(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8, %9, %10, %11, %12}, p;\n}\n" ::"r"(
+            tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u), "r"(0u),
+        "r"(0u), "r"(0u)
+        : "memory");
+}
+// completion of the issued MMAs arrives once on the barrier at this offset in both CTAs of the pair
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n" ::"r"(
+            bar),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+gemm2_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
+                const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K,
+                int epi) {
+    using C = Cfg2;
+    extern __shared__ unsigned char smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    unsigned char* gbase = smem_raw + (base - raw);
+    const uint32_t stg_base = base + C::STAGES * C::STAGE_BYTES;    // epilogue staging
+    const uint32_t bars = stg_base + C::STG_BYTES;
+    // barriers (same offsets in both CTAs): full[S] (leader: both CTAs' TMA bytes), empty[S],
+    // tfull[2], tempty[2] (leader: 2 x EPI_WARPS arrivals)
+    auto full_bar = [&](int s) { return bars + 8u * s; };
+    auto empty_bar = [&](int s) { return bars + 8u * (C::STAGES + s); };
+    auto tfull_bar = [&](int a) { return bars + 8u * (2 * C::STAGES + a); };
+    auto tempty_bar = [&](int a) { return bars + 8u * (2 * C::STAGES + 2 + a); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + (bars - base) + 8 * (2 * C::STAGES + 4));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const int num_k = cdiv(K, BK);
+    const int tiles_n = cdiv(N, BN2);
+    const int num_tiles = cdiv(M, BM2) * tiles_n;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; s++) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(tfull_bar(a), 1);
+            mbar_init(tempty_bar(a), 2 * EPI_WARPS);
+        }
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                     "r"((uint32_t)(2 * C::TMEM_COLS))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
+    }
+    tc_fence_before();
+    // both CTAs' barriers are initialised and their TMEM allocated before either CTA
+    // signals the other's barriers or the leader issues MMAs into it
+    cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            int g = 0;
+            for (int tile = pair; tile < num_tiles && !*abort_flag; tile += npairs) {
+                const int m0 = (tile / tiles_n) * BM2 + HALF * (int)rank;
+                const int n0 = (tile % tiles_n) * BN2 + HALF * (int)rank;
+                for (int i = 0; i < num_k; i++, g++) {
+                    const int s = g % C::STAGES;
+                    if (g >= C::STAGES && !mbar_wait(empty_bar(s), ((g / C::STAGES) - 1) & 1, abort_flag)) break;
+                    const uint32_t sa = base + s * C::STAGE_BYTES;
+                    const uint32_t lead_full = map_to_rank(full_bar(s), 0);
+                    if (rank == 0) mbar_expect_tx(full_bar(s), 2 * (C::A_BYTES + C::B_BYTES));
+                    tma_load_2d_pair(sa, &tmA, lead_full, i * BK, m0);
+                    tma_load_2d_pair(sa + C::A_BYTES, &tmB, lead_full, i * BK, n0);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ---------------- MMA issuer (the pair leader) ----------------
+            constexpr uint32_t idesc = idesc_i8_2sm();
+            int g = 0;
+            int it = 0;
+            for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
+                const int a = it & 1;
+                if (it >= 2 && !mbar_wait(tempty_bar(a), ((it >> 1) - 1) & 1, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t tacc = tmem + (uint32_t)(a * C::TMEM_COLS);
+                bool ok = true;
+                for (int i = 0; i < num_k; i++, g++) {
+                    const int s = g % C::STAGES;
+                    if (!mbar_wait(full_bar(s), (g / C::STAGES) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = base + s * C::STAGE_BYTES;
+                    const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+                    for (int kk = 0; kk < BK / 32; kk++)
+                        mma_i8_2sm(tacc, sdesc_sw128(sa + kk * 32), sdesc_sw128(sb + kk * 32), idesc, (i | kk) != 0);
+                    mma_commit_pair(empty_bar(s));
+                }
+                if (!ok) break;
+                mma_commit_pair(tfull_bar(a));
+            }
+        }
+    } else if (warp >= 2 && warp < 2 + EPI_WARPS) {
+        // ---------------- epilogue (both CTAs: each its 128 rows) ----------------
+        const int q = warp & 3;
+        const uint32_t stg = stg_base + (uint32_t)((warp - 2) * C::STG_BUFS * 4096);
+        unsigned char* stg_g = gbase + (stg - base);
+        const float ws = (epi == MI_EPI_F32_SCALED) ? *w_scale : 0.0f;
+        const float os = out_scale ? *out_scale : 1.0f;
+        int it = 0, nst = 0;
+        for (int tile = pair; tile < num_tiles; tile += npairs, it++) {
+            const int a = it & 1;
+            const bool have = __all_sync(0xffffffffu, mbar_wait(tfull_bar(a), (it >> 1) & 1, abort_flag));
+            if (!have) break;
+            tc_fence_after();
+            const int m0 = (tile / tiles_n) * BM2 + HALF * (int)rank;
+            const int n0 = (tile % tiles_n) * BN2;
+            const int row = m0 + q * 32 + lane;
+            float sc = 0.0f;
+            if (epi == MI_EPI_F32_SCALED && row < M) sc = __fmul_rn(ws, a_scale[row]);
+            const uint32_t tacc = tmem + (uint32_t)(a * C::TMEM_COLS) + ((uint32_t)(q * 32) << 16);
+#pragma unroll 1
+            for (int cb = 0; cb < C::EPI_BOXES; cb++, nst++) {
+                uint32_t r[32];
+                tmem_ld16(tacc + (uint32_t)(cb * 32), *reinterpret_cast<uint32_t(*)[16]>(&r[0]));
+                tmem_ld16(tacc + (uint32_t)(cb * 32 + 16), *reinterpret_cast<uint32_t(*)[16]>(&r[16]));
+                if (cb == C::EPI_BOXES - 1) {
+                    // every TMEM read of this accumulator is done: tell the leader's MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_cluster(map_to_rank(tempty_bar(a), 0));
+                }
+                if (epi == MI_EPI_F32_SCALED) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        float v = __fmul_rn((float)(int32_t)r[j], sc);
+                        if (out_scale) v = __fmul_rn(v, os);
+                        r[j] = __float_as_uint(v);
+                    }
+                }
+                if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(C::STG_BUFS - 1) : "memory");
+                __syncwarp();
+                unsigned char* rowp = stg_g + (nst & (C::STG_BUFS - 1)) * 4096 + lane * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    const int phys = c ^ (lane & 7);
+                    *reinterpret_cast<uint4*>(rowp + phys * 16) =
+                        make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+                }
+                asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+                __syncwarp();
+                if (lane == 0) {
+                    const int x = n0 + cb * 32, y = m0 + q * 32;
+                    if (x < N && y < M) tma_store_2d(&tmC, stg + (nst & (C::STG_BUFS - 1)) * 4096, x, y);
+                    asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+                }
+            }
+        }
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    // neither CTA frees TMEM or leaves while the other may still use the pair's resources
+    cluster_sync_all();
+    if (warp == 0) {
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(tmem),
+                     "r"((uint32_t)(2 * C::TMEM_COLS))
+                     : "memory");
+    }
+}
+
+static int launch2(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
+                   const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
+    CUtensorMap ta, tb, tc;
+    int rc = make_tmap(&ta, A, M, K, lda, BK, HALF, 1);
+    if (rc) return rc;
+    rc = make_wmap<false>(&tb, W, N, K, HALF);
+    if (rc) return rc;
+    rc = make_tmap(&tc, out, M, N, (long long)ldo * 4, 32, 32, 4);
+    if (rc) return rc;
+    using C = Cfg2;
+    if (cudaFuncSetAttribute(gemm2_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess) {
+        cudaGetLastError();
+        return MI_ERR_CUDA;
+    }
+    // as many pairs as can be resident at once (a GPC with an odd number of free SMs
+    // holds one pair fewer than half its SMs), so no pair waits for a second wave
+    static int resident = 0;
+    if (!resident) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (sm_count() / 2), 1, 1);
+        cfg.blockDim = dim3(THREADS, 1, 1);
+        cfg.dynamicSmemBytes = C::SMEM;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, gemm2_i8_kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = sm_count() / 2;
+        }
+        resident = n < sm_count() / 2 ? n : sm_count() / 2;
+    }
+    const int tiles = cdiv(M, BM2) * cdiv(N, BN2);
+    int pairs = resident;
+    if (pairs > tiles) pairs = tiles;
+    gemm2_i8_kernel<<<2 * pairs, THREADS, C::SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M, N, K, epi);
+    MI_CHECK_LAUNCH();
+    return MI_OK;
+}
+
 template <bool PACKED>
 static int launch_ares(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
                        const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s) {
@@ -880,6 +1180,16 @@ static int launch_ares(const int8_t* A, int lda, const void* W, const float* a_s
     return MI_OK;
 }
 
+// The 2-SM kernel for int8 weights and an output of N % 256 == 0 with at least one
+// 256 x 256 tile per SM pair; MI_GEMM_2SM=0 in the environment selects the one-CTA
+// kernels instead (read per call, for comparisons and tests).
+static bool use_pair_kernel(bool packed, int M, int N, int sms) {
+    if (packed) return false;
+    const char* e = getenv("MI_GEMM_2SM");
+    if (e && e[0] == '0') return false;
+    return N % BN2 == 0 && (long long)cdiv(M, BM2) * (N / BN2) >= sms / 2;
+}
+
 // Shape checks shared by both weight formats, then the kernel choice.
 template <bool PACKED>
 static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
@@ -898,6 +1208,10 @@ static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_sca
     const int sms = sm_count();
     const long long tm = cdiv(M, BM);
     auto fills = [&](int bn) { return tm * cdiv(N, bn) >= sms; };
+    // the pair kernel (256 x 256 tiles over two SMs) for int8 weights wherever N allows it
+    // and its tiles give every SM pair work
+    if (use_pair_kernel(PACKED, M, N, sms))
+        return launch2(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     // 256-wide tiles run the tensor cores at about twice the rate of 128-wide
     // ones; when N allows them they win even though A is then re-read from L2
     // for every N tile.  Otherwise wide outputs over a short K keep A resident.
@@ -1061,7 +1375,7 @@ static int bitlinear_norm_sqp(const int8_t* A, int lda, const uint8_t* Wp, const
     const long long tm = cdiv(M, BM);
     auto fills = [&](int bn) { return tm * cdiv(N, bn) >= sms; };
     int rc;
-    // the streaming kernel (whose epilogue adds the row sums), widest tile that fills the SMs
+    // the streaming kernel (its epilogue adds the row sums), widest tile that fills the SMs
     if (N <= 32) rc = launch<32, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
     else if (N <= 64) rc = launch<64, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
     else if (N <= 96) rc = launch<96, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);

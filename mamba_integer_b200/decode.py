@@ -78,13 +78,17 @@ class DecodeEngine:
     per token).  ``use_graph`` replays each step from a CUDA graph captured on
     the first step (the step launches no allocation and no host sync)."""
 
-    def __init__(self, model, prefill: PrefillEngine | None = None, use_graph: bool = True, fused: bool = True):
+    def __init__(self, model, prefill: PrefillEngine | None = None, use_graph: bool = True, fused: bool = True,
+                 packed_x: bool = True):
         self.pre = prefill if prefill is not None else PrefillEngine(model)
         self.n_layer = len(self.pre.layers)
         self.use_graph = use_graph
         # fused: one mid kernel per layer (mi_decode_mid); otherwise conv step,
         # x_proj GEMM and scan step as three launches
         self.fused = fused and self.pre.di % 16 == 0
+        # packed_x: the mid kernel reads x_proj's 2-bit packed weights (mi_decode_mid_packed)
+        self.packed_x = (packed_x and self.fused and self.pre.di % 64 == 0
+                         and all(p["w_x"].w2 is not None for p in self.pre.layers))
         self.states: StreamStates | None = None
         self.ws: _StepWorkspace | None = None
         self._graph = None
@@ -99,7 +103,10 @@ class DecodeEngine:
         kernels.rowprep(g0, s0, B, d, ids=ws.ids, emb=pre.emb, x_out=ws.x, xq=ws.xq_d, xscale=ws.xs_d)
         for i, p in enumerate(layers):
             ternary_matmul(ws.xq_d, p["w_in"], ws.xs_d, out=ws.xz)
-            if self.fused:
+            if self.fused and self.packed_x:
+                kernels.decode_mid_packed(ws.xz, p["conv_w"], p["conv_b"], st.win[i], p["w_x"].w2, p["w_x"].scale,
+                                          R, p["w_dt"].w8, p["w_dt"].scale, p["base"], st.h[i], ws.xq_i, ws.xs_i)
+            elif self.fused:
                 kernels.decode_mid(ws.xz, p["conv_w"], p["conv_b"], st.win[i], p["w_x"].w8, p["w_x"].scale, R,
                                    p["w_dt"].w8, p["w_dt"].scale, p["base"], st.h[i], ws.xq_i, ws.xs_i)
             else:

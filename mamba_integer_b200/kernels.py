@@ -334,6 +334,23 @@ def decode_mid(xz, conv_w, conv_b, win, w_x, w_x_scale, R: int, w_dt, w_dt_scale
                "mi_decode_mid")
 
 
+def decode_mid_packed(xz, conv_w, conv_b, win, w_x_packed, w_x_scale, R: int, w_dt, w_dt_scale, base, h, xq, xscale,
+                      xp_out=None):
+    """decode_mid with the x_proj weights in the 2-bit packed form (pack_ternary,
+    uint8 [R + 2N, D/4]); see mi_decode_mid_packed.  D % 64 == 0."""
+    batch = xz.shape[0]
+    D, N = base.shape
+    _need(w_x_packed, torch.uint8, "w_x_packed")
+    if tuple(w_x_packed.shape) != (R + 2 * N, D // 4) or not w_x_packed.is_contiguous():
+        raise ValueError(f"w_x_packed must be contiguous [{R + 2 * N}, {D // 4}]")
+    _lib.check(_lib.load().mi_decode_mid_packed(xz.data_ptr(), xz.stride(0), conv_w.data_ptr(), conv_b.data_ptr(),
+                                                win.data_ptr(), w_x_packed.data_ptr(), w_x_scale.data_ptr(), R,
+                                                w_dt.data_ptr(), w_dt_scale.data_ptr(), base.data_ptr(), h.data_ptr(),
+                                                _ptr(xp_out), xq.data_ptr(), xscale.data_ptr(), batch, D, N,
+                                                _stream()),
+               "mi_decode_mid_packed")
+
+
 def argmax_rows(x: torch.Tensor, V: Optional[int] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """torch.argmax(x[:, :V], dim=-1) as int64 (first index of the maximum, NaN highest)."""
     T = x.shape[0]

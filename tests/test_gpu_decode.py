@@ -136,10 +136,13 @@ def test_argmax_rows_ties_nan_and_inf(cuda_dev):
     assert got[5].item() == int(torch.argmax(x[5]))
 
 
-@pytest.mark.parametrize("D,R", [(80, 16), (256, 16), (2048, 64)])
+@pytest.mark.parametrize("D,R", [(80, 16), (256, 16), (576, 48), (2048, 64), (4096, 48)])
 def test_decode_mid_equals_unfused_step_kernels(cuda_dev, D, R):
     # mi_decode_mid (one CTA per stream for D % 64 != 0, a 4-CTA cluster per stream otherwise)
-    # against conv step -> x_proj GEMM -> scan step, each of which is checked against the oracle
+    # and mi_decode_mid_packed (the cluster kernel on 2-bit packed x_proj weights; D % 64 == 0)
+    # against conv step -> x_proj GEMM -> scan step, each of which is checked against the oracle.
+    # D = 576: threads of a CTA take 1 or 2 channels; 2048 / 4096: 4 / 8 channels each, so the
+    # cluster kernel's two-slot state prefetch wraps around
     from mamba_integer_b200 import kernels as k
     g = torch.Generator().manual_seed(D + R)
     B, N, P = 37, 16, R + 32
@@ -174,3 +177,19 @@ def test_decode_mid_equals_unfused_step_kernels(cuda_dev, D, R):
     assert torch.equal(h1.view(torch.int32), h2.view(torch.int32))
     assert torch.equal(yq1, yq2)
     assert torch.equal(ys1.view(torch.int32), ys2.view(torch.int32))
+    if D % 64 == 0:
+        win3, h3 = dv(win0.clone()), dv(h0.clone())
+        yq3, ys3 = torch.empty(B, D, dtype=torch.int8, device=cuda_dev), torch.empty(B, device=cuda_dev)
+        xp3 = torch.empty(B, P, device=cuda_dev)
+        k.decode_mid_packed(xz, cw, cb, win3, k.pack_ternary(w_x), w_x_scale, R, w_dt, w_dt_scale, base, h3, yq3, ys3,
+                            xp_out=xp3)
+        assert torch.equal(win1, win3)
+        assert torch.equal(xp.view(torch.int32), xp3.view(torch.int32))
+        assert torch.equal(h1.view(torch.int32), h3.view(torch.int32))
+        assert torch.equal(yq1, yq3)
+        assert torch.equal(ys1.view(torch.int32), ys3.view(torch.int32))
+    else:
+        from mamba_integer_b200._lib import MIError
+        with pytest.raises(MIError):
+            k.decode_mid_packed(xz, cw, cb, win2, torch.zeros(P, D // 4, dtype=torch.uint8, device=cuda_dev),
+                                w_x_scale, R, w_dt, w_dt_scale, base, h2, yq2, ys2)

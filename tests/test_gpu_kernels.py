@@ -349,6 +349,33 @@ def test_gemm_wide_tiles_both_weight_formats(cuda_dev, M, N, K):
     _eq(k.bitlinear_packed(Ad, k.pack_ternary(Wd), xsd, wsd), out_ref, "packed weights")
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 4096, 512), (4000, 4096, 320), (16384, 768, 1536), (1100, 32768, 768)])
+def test_gemm_pair_kernel_matches_oracle(cuda_dev, M, N, K, monkeypatch):
+    """The 2-SM kernel (tcgen05.mma.cta_group::2, 256 x 256 tiles over an SM pair), chosen
+    for int8 weights and N % 256 == 0 with a tile per pair: int32, scaled and
+    out_scale outputs, ragged M (a pair whose second half is past M), a K tail; the
+    one-CTA kernels (MI_GEMM_2SM=0, and packed weights always) give the same bits."""
+    k = _mi()
+    g = torch.Generator().manual_seed(M + N + K)
+    A = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int8)
+    W = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8)
+    xs = (torch.rand(M, generator=g) * 0.05 + 1e-3)
+    acc_ref = orc.gemm_i8_i32(A.numpy(), W.numpy())
+    out_ref = orc.bitlinear(A.numpy(), xs.numpy(), W.numpy(), 2.0 ** -6)
+    Ad, Wd, xsd = A.to(cuda_dev), W.to(cuda_dev), xs.to(cuda_dev)
+    wsd, osd = torch.tensor([2.0 ** -6], device=cuda_dev), torch.tensor([0.125], device=cuda_dev)
+    Wp = k.pack_ternary(Wd)
+    for pair in ("1", "0"):
+        monkeypatch.setenv("MI_GEMM_2SM", pair)
+        _eq(k.bitlinear_i8(Ad, Wd), acc_ref, f"int8 weights, int32 out, pair={pair}")
+        _eq(k.bitlinear_packed(Ad, Wp), acc_ref, f"packed weights, int32 out, pair={pair}")
+        _eq(k.bitlinear_packed(Ad, Wp, xsd, wsd), out_ref, f"packed weights, scaled out, pair={pair}")
+        scaled = k.bitlinear_i8(Ad, Wd, xsd, wsd, out_scale=osd).cpu().numpy()
+        _eq(scaled, (out_ref * np.float32(0.125)).astype(np.float32), f"int8 weights, out_scale, pair={pair}")
+    from mamba_integer_b200 import _lib
+    assert _lib.device_error() == 0
+
+
 def test_gemm_packed_config3_slice(cuda_dev):
     """Config-3 inputs with the weights packed 2 bits each: a 1024-row slice."""
     from mamba_integer_b200 import synth
