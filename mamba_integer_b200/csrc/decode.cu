@@ -100,6 +100,7 @@ conv_step_kernel(const float* __restrict__ xz, int ldx, const float* __restrict_
     const int b = blockIdx.x;
     const float* xrow = xz + (size_t)b * ldx;
     float* wrow = win + (size_t)b * 3 * D;
+    grid_dependency_sync();
     float4 a[CONV_CHUNKS];
     unsigned m = 0u;
 #pragma unroll
@@ -216,6 +217,7 @@ ssm_step_kernel(const float* __restrict__ act, const float* __restrict__ xp, int
     const int b = blockIdx.x;
     const float* row = xp + (size_t)b * ldxp;
     const int R16 = (R + 15) / 16 * 16;
+    grid_dependency_sync();
     if (threadIdx.x < 32) {
         dt_row_quant(row, R, R16, dtq_s, &dts_s);
         bc_s[threadIdx.x] = row[R + threadIdx.x];  // B (16) then C (16)
@@ -294,6 +296,7 @@ decode_mid_kernel(const float* __restrict__ xz, int ldx, const float* __restrict
     const int R16 = (R + 15) / 16 * 16;
     const float* xrow = xz + (size_t)b * ldx;
     float* wrow = win + (size_t)b * 3 * D;
+    grid_dependency_sync();
 
     // (1) conv + activation on this thread's chunks of 4 channels (into shared memory)
     float4 a[MID_CONV];
@@ -473,6 +476,7 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     const float* xrow = xz + (size_t)b * ldx;
     float* wrow = win + (size_t)b * 3 * D;
     float* hbase = h + ((size_t)b * D + c0) * NS;  // this CTA's state rows
+    grid_dependency_sync();
     const float wxs = *w_x_scale, wdts = *w_dt_scale;
 
     // (1) conv + activation of this CTA's channels, into shared memory
@@ -636,6 +640,7 @@ argmax_rows_kernel(const float* __restrict__ x, int ldx, int V, int64_t* __restr
     __shared__ float sv[ARGMAX_THREADS / 32];
     __shared__ int si[ARGMAX_THREADS / 32];
     const float* row = x + (size_t)blockIdx.x * ldx;
+    grid_dependency_sync();
     const float ninf = -__int_as_float(0x7f800000);
     float bv = ninf;
     int bi = 0x7fffffff;
@@ -709,8 +714,8 @@ extern "C" int mi_conv_step(const float* xz, int ldx, const float* w, const floa
     if (D % 4 != 0 || D > MAX_D || ldx % 4 != 0 || batch > 2147483647 / 4) return MI_ERR_UNSUPPORTED;
     if (((uintptr_t)xz | (uintptr_t)w | (uintptr_t)bias | (uintptr_t)win | (uintptr_t)act) & 15) return MI_ERR_INVALID;
     if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
-    conv_step_kernel<<<batch, STEP_THREADS, 0, (cudaStream_t)stream>>>(xz, ldx, w, bias, win, act, xq, xscale, D);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(conv_step_kernel, dim3(batch), dim3(STEP_THREADS), 0, (cudaStream_t)stream, xz, ldx, w, bias,
+                        win, act, xq, xscale, D);
     return MI_OK;
 }
 
@@ -723,9 +728,8 @@ extern "C" int mi_ssm_step(const float* act, const float* xp, int ldxp, int R, c
     if (batch <= 0 || D <= 0 || R <= 0 || ldxp < R + 2 * N || ldz < D) return MI_ERR_INVALID;
     if (D > MAX_D || (R + 15) / 16 * 16 > MAX_R16) return MI_ERR_UNSUPPORTED;
     if (((uintptr_t)h | (uintptr_t)base | (uintptr_t)w_dt) & 15) return MI_ERR_INVALID;
-    ssm_step_kernel<<<batch, STEP_THREADS, 0, (cudaStream_t)stream>>>(act, xp, ldxp, R, w_dt, w_dt_scale, z, ldz, base,
-                                                                     h, y, xq, xscale, D);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(ssm_step_kernel, dim3(batch), dim3(STEP_THREADS), 0, (cudaStream_t)stream, act, xp, ldxp, R,
+                        w_dt, w_dt_scale, z, ldz, base, h, y, xq, xscale, D);
     return MI_OK;
 }
 
@@ -746,14 +750,13 @@ extern "C" int mi_decode_mid(const float* xz, int ldx, const float* conv_w, cons
     if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
     if (D % (16 * MC_CS) == 0 && (long long)batch * MC_CS <= 0x7fffffffLL) {
         // a cluster of MC_CS CTAs per stream (each channel slice a multiple of 16 bytes of int8)
-        decode_mid_cluster_kernel<false><<<batch * MC_CS, MC_THREADS, 0, (cudaStream_t)stream>>>(
-            xz, ldx, conv_w, conv_b, win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
+        MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<false>, dim3(batch * MC_CS), dim3(MC_THREADS), 0,
+                            (cudaStream_t)stream, xz, ldx, conv_w, conv_b, win, (const void*)w_x, w_x_scale, R, w_dt,
+                            w_dt_scale, base, h, xp_out, xq, xscale, D);
     } else {
-        decode_mid_kernel<<<batch, MID_THREADS, 0, (cudaStream_t)stream>>>(xz, ldx, conv_w, conv_b, win, w_x,
-                                                                            w_x_scale, R, w_dt, w_dt_scale, base, h,
-                                                                            xp_out, xq, xscale, D);
+        MI_LAUNCH_DEPENDENT(decode_mid_kernel, dim3(batch), dim3(MID_THREADS), 0, (cudaStream_t)stream, xz, ldx,
+                            conv_w, conv_b, win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
     }
-    MI_CHECK_LAUNCH();
     return MI_OK;
 }
 
@@ -775,16 +778,15 @@ extern "C" int mi_decode_mid_packed(const float* xz, int ldx, const float* conv_
          (uintptr_t)w_dt) & 15)
         return MI_ERR_INVALID;
     if (((uintptr_t)w_x_packed | (uintptr_t)xq) & 3) return MI_ERR_INVALID;
-    decode_mid_cluster_kernel<true><<<batch * MC_CS, MC_THREADS, 0, (cudaStream_t)stream>>>(
-        xz, ldx, conv_w, conv_b, win, w_x_packed, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<true>, dim3(batch * MC_CS), dim3(MC_THREADS), 0,
+                        (cudaStream_t)stream, xz, ldx, conv_w, conv_b, win, (const void*)w_x_packed, w_x_scale, R,
+                        w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
     return MI_OK;
 }
 
 extern "C" int mi_argmax_rows(const float* x, int ldx, int T, int V, int64_t* out, void* stream) {
     using namespace mi::decode;
     if (!x || !out || T <= 0 || V <= 0 || ldx < V) return MI_ERR_INVALID;
-    argmax_rows_kernel<<<T, ARGMAX_THREADS, 0, (cudaStream_t)stream>>>(x, ldx, V, out);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(argmax_rows_kernel, dim3(T), dim3(ARGMAX_THREADS), 0, (cudaStream_t)stream, x, ldx, V, out);
     return MI_OK;
 }

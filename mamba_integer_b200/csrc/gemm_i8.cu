@@ -272,6 +272,9 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    // the previous kernel's outputs (A, the scales) are complete and its TMEM is
+    // free before this CTA allocates TMEM or loads anything
+    grid_dependency_sync();
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                      "r"((uint32_t)(2 * C::TMEM_COLS))
@@ -565,6 +568,7 @@ gemm_i8_ares_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
+    grid_dependency_sync();  // as in gemm_i8_kernel
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                      "r"((uint32_t)(2 * TMEM_COLS))
@@ -836,9 +840,8 @@ static int launch(const int8_t* A, int lda, const void* W, const float* a_scale,
     }
     const int tiles = cdiv(M, BM) * cdiv(N, BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    gemm_i8_kernel<BN, PACKED><<<grid, threads_of<PACKED>(), C::SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale,
-                                                                         M, N, K, epi, row_stats);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(gemm_i8_kernel<BN, PACKED>, dim3(grid), dim3(threads_of<PACKED>()), C::SMEM, s, ta, tb, tc,
+                        a_scale, w_scale, out_scale, M, N, K, epi, row_stats);
     return MI_OK;
 }
 
@@ -1174,9 +1177,8 @@ static int launch_ares(const int8_t* A, int lda, const void* W, const float* a_s
     if (groups > tiles_n) groups = tiles_n;
     const int units = tiles_m * groups;
     const int grid = units < sms ? units : sms;
-    gemm_i8_ares_kernel<PACKED><<<grid, threads_of<PACKED>(), SMEM, s>>>(ta, tb, tc, a_scale, w_scale, out_scale, M,
-                                                                        N, K, epi, groups);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(gemm_i8_ares_kernel<PACKED>, dim3(grid), dim3(threads_of<PACKED>()), SMEM, s, ta, tb, tc,
+                        a_scale, w_scale, out_scale, M, N, K, epi, groups);
     return MI_OK;
 }
 

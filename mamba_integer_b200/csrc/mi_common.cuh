@@ -9,6 +9,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
 #include <cuda_runtime.h>
 
 #include "../../include/mi_b200.h"
@@ -215,10 +216,57 @@ __device__ __forceinline__ int quant_i8(float v) {
 // ceil(a / b) for positive ints
 __host__ __device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// Programmatic dependent launch.  A kernel started by launch_dependent() may
+// begin while the kernel before it in the stream is still finishing (its
+// launch and prologue overlap that kernel's tail).  Such a kernel calls
+// grid_dependency_sync() before its first access to global memory that an
+// earlier kernel writes, or reads and this kernel then overwrites: it returns
+// once every earlier kernel has completed and its writes are visible.  The
+// kernel then lets its own successor start launching; as that successor
+// waits in the same way, at most two kernels of the stream overlap.  In a
+// kernel launched without the attribute both instructions have nothing to
+// wait for.
+__device__ __forceinline__ void grid_dependency_sync() {
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+// MI_PDL=0 in the environment launches every kernel fully serialised (read
+// per launch, for comparisons and tests).
+static inline bool pdl_enabled() {
+    const char* e = getenv("MI_PDL");
+    return !(e && e[0] == '0');
+}
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                           cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 }  // namespace mi
 
 #define MI_CHECK_LAUNCH()                                   \
     do {                                                    \
         cudaError_t e_ = cudaGetLastError();                \
         if (e_ != cudaSuccess) return MI_ERR_CUDA;          \
+    } while (0)
+
+// mi::launch_dependent(kernel, grid, block, smem, stream, args...) or return MI_ERR_CUDA
+#define MI_LAUNCH_DEPENDENT(...)                                   \
+    do {                                                           \
+        if (mi::launch_dependent(__VA_ARGS__) != cudaSuccess) {    \
+            cudaGetLastError();                                    \
+            return MI_ERR_CUDA;                                    \
+        }                                                          \
     } while (0)

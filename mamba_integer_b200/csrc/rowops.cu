@@ -80,6 +80,7 @@ rowprep_kernel(const float* x, const float* delta, const float* __restrict__ res
     constexpr int D = 32 * R;
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
+    grid_dependency_sync();
     const float g = (mode & 2) ? *res_gate : 0.0f;
     const float stp = *step;
     float gam[R];
@@ -255,9 +256,8 @@ static int launch_rowprep(const float* x, const float* delta, const float* res_g
     const int threads = 256;
     int blocks = cdiv(T, threads / 32);
     if (blocks > 148 * 16) blocks = 148 * 16;
-    fn<<<blocks, threads, 0, s>>>(x, delta, res_gate, ids, emb, vocab, x_out, gamma, step, y_norm, xq, xscale, inv_rms, T,
-                                  mode);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(fn, dim3(blocks), dim3(threads), 0, s, x, delta, res_gate, ids, emb, vocab, x_out, gamma, step,
+                        y_norm, xq, xscale, inv_rms, T, mode);
     return MI_OK;
 }
 
