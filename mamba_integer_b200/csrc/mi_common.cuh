@@ -232,10 +232,14 @@ __device__ __forceinline__ void grid_dependency_sync() {
 }
 
 // MI_PDL=0 in the environment launches every kernel fully serialised (read
-// per launch, for comparisons and tests).
+// once per process, at the first launch: a getenv per launch costs host time
+// in the eager, launch-bound paths).
 static inline bool pdl_enabled() {
-    const char* e = getenv("MI_PDL");
-    return !(e && e[0] == '0');
+    static const bool on = [] {
+        const char* e = getenv("MI_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 template <typename... KArgs, typename... Args>
