@@ -385,14 +385,15 @@ decode_mid_kernel(const float* __restrict__ xz, int ldx, const float* __restrict
 // one 512-thread CTA per stream left most SMs with one or two.
 // 4 CTAs of 128 threads per stream measured fastest at config 5 (256 streams, d_inner 2048):
 // 1.51 ms per decode step, against 1.57 for one 512-thread CTA per stream, 1.57 for 2 x 128,
-// 1.62 for 4 x 64, 1.73 for 4 x 256, 1.78 for 8 x 128
+// 1.62 for 4 x 64, 1.73 for 4 x 256, 1.78 for 8 x 128.
+// NT threads a CTA: held to 64 registers, an SM keeps 1024 of them, so the launch
+// takes the widest NT (fewest channels a thread walks in series) whose
+// batch x 4 x NT threads are still one wave: 128 at 256 streams, 256 at 128, 512 below.
 constexpr int MC_CS = 4;          // CTAs per stream (a portable cluster size)
-constexpr int MC_THREADS = 128;
 constexpr int MC_XO = 4;          // x_proj outputs per warp pass (int8 weights)
 constexpr int MC_XOP = 12;        // x_proj outputs per warp pass (2-bit packed weights)
 constexpr int MC_MAX_DC = MAX_D / MC_CS;
-// at most 64 registers a thread: 8 CTAs per SM, so 256 streams (1024 CTAs) are one wave
-constexpr int MC_MIN_CTAS = 8;
+constexpr int MC_SM_THREADS = 1024;  // threads an SM keeps at 64 registers
 
 // One channel of the scan step with its 16 states already in registers (hv4,
 // updated in place; the caller stores them): dt_proj, decay / dt / u, the
@@ -446,8 +447,8 @@ __device__ __forceinline__ float ssm_channel_update(int c, float actv, float zv,
 // PACKED_X: w_x is the 2-bit packed form [R + 2N, D/4] (pack_ternary's layout)
 // instead of int8 [R + 2N, D]; a quarter of the bytes for every stream's CTAs
 // to read, and each lane loads its weight words for MC_XOP outputs at once.
-template <bool PACKED_X>
-__global__ void __cluster_dims__(MC_CS, 1, 1) __launch_bounds__(MC_THREADS, MC_MIN_CTAS)
+template <bool PACKED_X, int NT>
+__global__ void __cluster_dims__(MC_CS, 1, 1) __launch_bounds__(NT, MC_SM_THREADS / NT)
 decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __restrict__ cw,
                           const float* __restrict__ cb, float* __restrict__ win, const void* __restrict__ w_x_any,
                           const float* __restrict__ w_x_scale, int R, const int8_t* __restrict__ w_dt,
@@ -456,7 +457,7 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
                           float* __restrict__ xscale, int D) {
     namespace cg = cooperative_groups;
     constexpr int NS = 16;
-    constexpr int NW = MC_THREADS / 32;
+    constexpr int NW = NT / 32;
     __shared__ __align__(16) float act_s[MC_MAX_DC];
     __shared__ __align__(16) int8_t xq_s[MC_MAX_DC];
     __shared__ float xp_s[MAX_P];
@@ -481,12 +482,12 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
 
     // (1) conv + activation of this CTA's channels, into shared memory
     unsigned m = 0u;
-    for (int i = threadIdx.x; i < DC / 4; i += MC_THREADS) {
+    for (int i = threadIdx.x; i < DC / 4; i += NT) {
         const float4 a = conv_chunk_step(xrow, wrow, cw, cb, c0 + 4 * i, D);
         m = max(m, absmax_bits4(a));
         *reinterpret_cast<float4*>(act_s + 4 * i) = a;
     }
-    m = block_max_bits<MC_THREADS>(m, red);
+    m = block_max_bits<NT>(m, red);
     if (threadIdx.x == 0) part_amax = m;
     cluster.sync();
     // (2) the row's absmax from every CTA's partial, then this CTA's int8 values
@@ -495,7 +496,7 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     for (int r = 0; r < MC_CS; r++) am = max(am, *cluster.map_shared_rank(&part_amax, r));
     float xs_c;
     const float inv_c = quant_inv(__uint_as_float(am), xs_c);
-    for (int i = threadIdx.x; i < DC / 4; i += MC_THREADS)
+    for (int i = threadIdx.x; i < DC / 4; i += NT)
         *reinterpret_cast<char4*>(xq_s + 4 * i) = quant4(*reinterpret_cast<const float4*>(act_s + 4 * i), inv_c);
     __syncthreads();
     // (3) x_proj: exact int32 partial dot products over this CTA's channels, summed across the
@@ -569,7 +570,7 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     }
     cluster.sync();
     const float sc_x = __fmul_rn(wxs, xs_c);  // (w_scale * x_scale), as the GEMM epilogue
-    for (int o = threadIdx.x; o < P; o += MC_THREADS) {
+    for (int o = threadIdx.x; o < P; o += NT) {
         int acc = 0;
 #pragma unroll
         for (int r = 0; r < MC_CS; r++) acc += *cluster.map_shared_rank(&part_xp[o], r);
@@ -586,7 +587,7 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     // the next channels' states in shared memory by cp.async was slower: the smem it takes
     // comes out of the L1 that holds the weights every stream's CTAs read.)
     unsigned my = 0u;
-    for (int i = threadIdx.x; i < DC; i += MC_THREADS) {
+    for (int i = threadIdx.x; i < DC; i += NT) {
         const int c = c0 + i;
         float4* hp = reinterpret_cast<float4*>(hbase + (size_t)i * NS);
         float4 hv4[NS / 4];
@@ -598,7 +599,7 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
         act_s[i] = yv;
         my = max(my, __float_as_uint(fabsf(yv)));
     }
-    my = block_max_bits<MC_THREADS>(my, red);
+    my = block_max_bits<NT>(my, red);
     if (threadIdx.x == 0) part_ymax = my;
     cluster.sync();
     // (6) y's absmax over the cluster, then the int8 values of this CTA's channels
@@ -607,11 +608,36 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     for (int r = 0; r < MC_CS; r++) ym = max(ym, *cluster.map_shared_rank(&part_ymax, r));
     float xs_y;
     const float inv_y = quant_inv(__uint_as_float(ym), xs_y);
-    for (int i = threadIdx.x; i < DC; i += MC_THREADS)
+    for (int i = threadIdx.x; i < DC; i += NT)
         xq[(size_t)b * D + c0 + i] = (int8_t)quant_i8(__fmul_rn(act_s[i], inv_y));
     if (threadIdx.x == 0 && rank == 0) xscale[b] = xs_y;
     // no CTA leaves while another may still read its shared memory
     cluster.sync();
+}
+
+// The cluster kernel at the widest CTA (at most one thread per channel of its
+// slice) whose batch x MC_CS CTAs fit the SMs in one wave, with a sixteenth of
+// the SMs kept in reserve for the ones a cluster layout leaves idle.
+template <bool PACKED_X>
+static int launch_mid_cluster(const float* xz, int ldx, const float* conv_w, const float* conv_b, float* win,
+                              const void* w_x, const float* w_x_scale, int R, const int8_t* w_dt,
+                              const float* w_dt_scale, const float* base, float* h, float* xp_out, int8_t* xq,
+                              float* xscale, int batch, int D, cudaStream_t s) {
+    const long long room = (long long)mi::gemm::sm_count() * MC_SM_THREADS * 15 / 16;
+    const long long ctas = (long long)batch * MC_CS;
+    const int DC = D / MC_CS;
+    const dim3 grid((unsigned)ctas);
+    if (ctas * 512 <= room && DC >= 512) {
+        MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<PACKED_X, 512>, grid, dim3(512), 0, s, xz, ldx, conv_w, conv_b,
+                            win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
+    } else if (ctas * 256 <= room && DC >= 256) {
+        MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<PACKED_X, 256>, grid, dim3(256), 0, s, xz, ldx, conv_w, conv_b,
+                            win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
+    } else {
+        MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<PACKED_X, 128>, grid, dim3(128), 0, s, xz, ldx, conv_w, conv_b,
+                            win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
+    }
+    return MI_OK;
 }
 
 // torch.argmax over each row: the first index of the maximum, NaN above
@@ -750,9 +776,8 @@ extern "C" int mi_decode_mid(const float* xz, int ldx, const float* conv_w, cons
     if (((uintptr_t)xq) & 3) return MI_ERR_INVALID;
     if (D % (16 * MC_CS) == 0 && (long long)batch * MC_CS <= 0x7fffffffLL) {
         // a cluster of MC_CS CTAs per stream (each channel slice a multiple of 16 bytes of int8)
-        MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<false>, dim3(batch * MC_CS), dim3(MC_THREADS), 0,
-                            (cudaStream_t)stream, xz, ldx, conv_w, conv_b, win, (const void*)w_x, w_x_scale, R, w_dt,
-                            w_dt_scale, base, h, xp_out, xq, xscale, D);
+        return launch_mid_cluster<false>(xz, ldx, conv_w, conv_b, win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h,
+                                         xp_out, xq, xscale, batch, D, (cudaStream_t)stream);
     } else {
         MI_LAUNCH_DEPENDENT(decode_mid_kernel, dim3(batch), dim3(MID_THREADS), 0, (cudaStream_t)stream, xz, ldx,
                             conv_w, conv_b, win, w_x, w_x_scale, R, w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
@@ -778,10 +803,8 @@ extern "C" int mi_decode_mid_packed(const float* xz, int ldx, const float* conv_
          (uintptr_t)w_dt) & 15)
         return MI_ERR_INVALID;
     if (((uintptr_t)w_x_packed | (uintptr_t)xq) & 3) return MI_ERR_INVALID;
-    MI_LAUNCH_DEPENDENT(decode_mid_cluster_kernel<true>, dim3(batch * MC_CS), dim3(MC_THREADS), 0,
-                        (cudaStream_t)stream, xz, ldx, conv_w, conv_b, win, (const void*)w_x_packed, w_x_scale, R,
-                        w_dt, w_dt_scale, base, h, xp_out, xq, xscale, D);
-    return MI_OK;
+    return launch_mid_cluster<true>(xz, ldx, conv_w, conv_b, win, w_x_packed, w_x_scale, R, w_dt, w_dt_scale, base,
+                                    h, xp_out, xq, xscale, batch, D, (cudaStream_t)stream);
 }
 
 extern "C" int mi_argmax_rows(const float* x, int ldx, int T, int V, int64_t* out, void* stream) {

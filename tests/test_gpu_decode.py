@@ -136,16 +136,18 @@ def test_argmax_rows_ties_nan_and_inf(cuda_dev):
     assert got[5].item() == int(torch.argmax(x[5]))
 
 
-@pytest.mark.parametrize("D,R", [(80, 16), (256, 16), (576, 48), (2048, 64), (4096, 48)])
-def test_decode_mid_equals_unfused_step_kernels(cuda_dev, D, R):
+@pytest.mark.parametrize("D,R,B", [(80, 16, 37), (256, 16, 37), (576, 48, 37), (2048, 64, 37), (4096, 48, 37),
+                                   (2048, 64, 100), (2048, 64, 256)])
+def test_decode_mid_equals_unfused_step_kernels(cuda_dev, D, R, B):
     # mi_decode_mid (one CTA per stream for D % 64 != 0, a 4-CTA cluster per stream otherwise)
     # and mi_decode_mid_packed (the cluster kernel on 2-bit packed x_proj weights; D % 64 == 0)
     # against conv step -> x_proj GEMM -> scan step, each of which is checked against the oracle.
-    # D = 576: threads of a CTA take 1 or 2 channels; 2048 / 4096: 4 / 8 channels each, so the
-    # cluster kernel's two-slot state prefetch wraps around
+    # The cluster kernel's CTA width follows the stream count: 37 streams at D = 2048 / 4096 run
+    # 512-thread CTAs (1 / 2 channels a thread), 100 streams 256 threads, 256 streams 128
+    # threads (4 channels a thread); D = 576 and 256 run 128 threads with some of them idle
     from mamba_integer_b200 import kernels as k
-    g = torch.Generator().manual_seed(D + R)
-    B, N, P = 37, 16, R + 32
+    g = torch.Generator().manual_seed(D + R + B)
+    N, P = 16, R + 32
     R16 = (R + 15) // 16 * 16
     dv = lambda t: t.to(cuda_dev)  # noqa: E731
     xz = dv(torch.randn(B, 2 * D, generator=g) * 2)
