@@ -15,6 +15,13 @@ fixed set of stream slots resident on the GPU (conv windows and scan states of
     `eos_id`; its slot is free for the next admission (stale state there is
     overwritten by the next prefill; idle slots are computed and ignored).
 
+The host runs one step behind the GPU: a call launches step t (its next ids
+stay on the device as step t+1's input and are copied to pinned host memory
+behind an event), then reads step t-1's ids and does the bookkeeping while
+step t runs.  A request that finished at step t-1 has had step t computed for
+its slot too; that token is dropped (each slot's step is credited only to the
+request that held the slot when the step was launched and still holds it).
+
 Every request gets exactly the tokens greedy full-recompute generation gives
 its prompt alone: streams never interact (every operation is per stream), so
 neither the other slots nor the admission time change a stream's bits.
@@ -50,6 +57,12 @@ class DecodeServer:
         self.finished: Dict[int, List[int]] = {}
         self._next_rid = 0
         self.steps = 0
+        # two pinned buffers for the next ids of the last two launched steps, each
+        # with the event its device-to-host copy completes; the launched step whose
+        # ids are not read yet, with the slot owners at its launch
+        self._host_ids = [torch.empty(slots, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+        self._ready = [torch.cuda.Event() for _ in range(2)]
+        self._inflight = None
 
     def submit(self, prompt: Sequence[int], max_new_tokens: int) -> int:
         if len(prompt) == 0 or max_new_tokens <= 0:
@@ -60,7 +73,7 @@ class DecodeServer:
         return rid
 
     def pending(self) -> int:
-        return len(self.queue) + sum(r is not None for r in self.active)
+        return len(self.queue) + sum(r is not None for r in self.active) + (self._inflight is not None)
 
     # -- internals -------------------------------------------------------------
     def _append(self, slot: int, tok: int) -> None:
@@ -93,25 +106,37 @@ class DecodeServer:
                 self._append(s, tok)
             free = [i for i, r in enumerate(self.active) if r is None]
 
+    def _consume(self, k: int, owners: List[Optional[Request]]) -> None:
+        """Credit a launched step's ids (pinned buffer k) to the slots' owners at launch."""
+        self._ready[k].synchronize()
+        toks = self._host_ids[k].tolist()
+        for s, r in enumerate(owners):
+            if r is not None and self.active[s] is r:
+                self._append(s, toks[s])
+
     # -- public loop -------------------------------------------------------------
     def step(self) -> bool:
-        """Admit what fits, then run one decode step; False when nothing is left."""
+        """Admit what fits, launch one decode step if any slot is active, then do the
+        previous step's bookkeeping; False when nothing is left."""
         self._admit()
-        if all(r is None for r in self.active):
-            return bool(self.queue)
-        ws = self.eng.ws
-        self.eng.step(ws.ids)
-        nxt = self.eng.next_ids()
-        toks = nxt.tolist()  # one device-to-host copy per step
-        ws.ids.copy_(nxt)    # every slot's next input is its own last token
-        self.steps += 1
-        for s, r in enumerate(self.active):
-            if r is not None:
-                self._append(s, toks[s])
-        return True
+        launched = None
+        if any(r is not None for r in self.active):
+            ws = self.eng.ws
+            self.eng.step(ws.ids)
+            nxt = self.eng.next_ids()
+            ws.ids.copy_(nxt)  # every slot's next input is its own last token
+            k = self.steps & 1
+            self._host_ids[k].copy_(nxt, non_blocking=True)
+            self._ready[k].record()
+            launched = (k, list(self.active))
+            self.steps += 1
+        if self._inflight is not None:
+            self._consume(*self._inflight)
+        self._inflight = launched
+        return self.pending() > 0
 
     def run(self) -> Dict[int, List[int]]:
         """Serve until every submitted request has finished."""
-        while self.step() or self.pending():
+        while self.step():
             pass
         return self.finished
