@@ -7,12 +7,12 @@ kernels over that cached state:
 
     rowprep      embedding gather (+ residual later) + BitShiftNorm + int8 quant  [B, d]
     per layer:
-      in_proj    tcgen05 GEMM from 2-bit packed weights  -> xz        [B, 2di]
-      mid        one kernel, one CTA per stream: conv window + ste_clamp +
-                 squareplus + int8 quant; x_proj as int8 dot products; dt
-                 quant + dt_proj + decay/dt/u + one state update + h.C + gate
-                 + int8 quant                                          [B, di]
-      out_proj   tcgen05 GEMM                            -> out       [B, d]
+      in_proj    tcgen05 GEMM from int8 weights          -> xz        [B, 2di]
+      mid        one kernel, a 4-CTA cluster per stream: conv window +
+                 ste_clamp + squareplus + int8 quant; x_proj as int8 dot
+                 products on 2-bit packed weights; dt quant + dt_proj +
+                 decay/dt/u + one state update + h.C + gate + int8 quant [B, di]
+      out_proj   tcgen05 GEMM from int8 weights          -> out       [B, d]
       rowprep    residual += out*res_gate, next norm + quant
     lm_head GEMM, argmax -> next token ids
 
@@ -89,6 +89,14 @@ class DecodeEngine:
         # packed_x: the mid kernel reads x_proj's 2-bit packed weights (mi_decode_mid_packed)
         self.packed_x = (packed_x and self.fused and self.pre.di % 64 == 0
                          and all(p["w_x"].w2 is not None for p in self.pre.layers))
+        # The step's GEMMs (one row per stream) read the int8 copies of the weights:
+        # at a few hundred rows they are latency-bound, and the packed form's unpack
+        # hand-off lengthens every K-slice, while the 4x weight bytes cost ~20 us of
+        # HBM per step (256 streams, config 5: 1.48 -> 1.41 ms per step).  The
+        # prompt prefill keeps the packed weights.
+        i8 = lambda tw: tw._replace(w2=None)  # noqa: E731
+        self._step_w = [(i8(p["w_in"]), i8(p["w_x"]), i8(p["w_out"])) for p in self.pre.layers]
+        self._step_lm = i8(self.pre.w_lm)
         self.states: StreamStates | None = None
         self.ws: _StepWorkspace | None = None
         self._graph = None
@@ -102,7 +110,8 @@ class DecodeEngine:
         g0, s0 = (layers[0]["gamma"], layers[0]["step"]) if layers else (pre.gamma_f, pre.step_f)
         kernels.rowprep(g0, s0, B, d, ids=ws.ids, emb=pre.emb, x_out=ws.x, xq=ws.xq_d, xscale=ws.xs_d)
         for i, p in enumerate(layers):
-            ternary_matmul(ws.xq_d, p["w_in"], ws.xs_d, out=ws.xz)
+            w_in, w_x, w_out = self._step_w[i]
+            ternary_matmul(ws.xq_d, w_in, ws.xs_d, out=ws.xz)
             if self.fused and self.packed_x:
                 kernels.decode_mid_packed(ws.xz, p["conv_w"], p["conv_b"], st.win[i], p["w_x"].w2, p["w_x"].scale,
                                           R, p["w_dt"].w8, p["w_dt"].scale, p["base"], st.h[i], ws.xq_i, ws.xs_i)
@@ -111,15 +120,15 @@ class DecodeEngine:
                                    p["w_dt"].w8, p["w_dt"].scale, p["base"], st.h[i], ws.xq_i, ws.xs_i)
             else:
                 kernels.conv_step(ws.xz, p["conv_w"], p["conv_b"], st.win[i], di, ws.xq_i, ws.xs_i, act=ws.act)
-                ternary_matmul(ws.xq_i, p["w_x"], ws.xs_i, out=ws.xp)
+                ternary_matmul(ws.xq_i, w_x, ws.xs_i, out=ws.xp)
                 kernels.ssm_step(ws.act, ws.xp, R, p["w_dt"].w8, p["w_dt"].scale, ws.xz[:, di:], p["base"],
                                  st.h[i], ws.xq_i, ws.xs_i)
-            ternary_matmul(ws.xq_i, p["w_out"], ws.xs_i, out=ws.out)
+            ternary_matmul(ws.xq_i, w_out, ws.xs_i, out=ws.out)
             nxt = layers[i + 1] if i + 1 < len(layers) else None
             g, s = (nxt["gamma"], nxt["step"]) if nxt else (pre.gamma_f, pre.step_f)
             kernels.rowprep(g, s, B, d, x=ws.x, delta=ws.out, res_gate=p["res_gate"], x_out=ws.x, xq=ws.xq_d,
                             xscale=ws.xs_d)
-        ternary_matmul(ws.xq_d, pre.w_lm, ws.xs_d, out_scale=pre.out_scale, out=ws.logits)
+        ternary_matmul(ws.xq_d, self._step_lm, ws.xs_d, out_scale=pre.out_scale, out=ws.logits)
         kernels.argmax_rows(ws.logits, out=ws.next_ids)
 
     def launches_per_step(self) -> int:

@@ -60,8 +60,10 @@ class DecodeServer:
         # two pinned buffers for the next ids of the last two launched steps, each
         # with the event its device-to-host copy completes; the launched step whose
         # ids are not read yet, with the slot owners at its launch
-        self._host_ids = [torch.empty(slots, dtype=torch.int64, pin_memory=True) for _ in range(2)]
-        self._ready = [torch.cuda.Event() for _ in range(2)]
+        # (an engine whose ids live on the host -- a stand-in for host tests -- needs neither)
+        on_gpu = self.eng.ws.ids.is_cuda
+        self._host_ids = [torch.empty(slots, dtype=torch.int64, pin_memory=on_gpu) for _ in range(2)]
+        self._ready = [torch.cuda.Event() if on_gpu else None for _ in range(2)]
         self._inflight = None
 
     def submit(self, prompt: Sequence[int], max_new_tokens: int) -> int:
@@ -108,7 +110,8 @@ class DecodeServer:
 
     def _consume(self, k: int, owners: List[Optional[Request]]) -> None:
         """Credit a launched step's ids (pinned buffer k) to the slots' owners at launch."""
-        self._ready[k].synchronize()
+        if self._ready[k] is not None:
+            self._ready[k].synchronize()
         toks = self._host_ids[k].tolist()
         for s, r in enumerate(owners):
             if r is not None and self.active[s] is r:
@@ -126,8 +129,9 @@ class DecodeServer:
             nxt = self.eng.next_ids()
             ws.ids.copy_(nxt)  # every slot's next input is its own last token
             k = self.steps & 1
-            self._host_ids[k].copy_(nxt, non_blocking=True)
-            self._ready[k].record()
+            self._host_ids[k].copy_(nxt, non_blocking=self._ready[k] is not None)
+            if self._ready[k] is not None:
+                self._ready[k].record()
             launched = (k, list(self.active))
             self.steps += 1
         if self._inflight is not None:
