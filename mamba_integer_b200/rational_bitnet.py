@@ -58,12 +58,32 @@ class TernaryWeights(NamedTuple):
     scale: torch.Tensor         # fp32 [1]: the AbsMean scale
 
 
+_SM_PAIRS: dict = {}
+
+
+def _pair_kernel_wins(M: int, N: int, K: int, dev: torch.device) -> bool:
+    """A GEMM heavy enough in K for the tensor cores to set its pace (K >= 1536),
+    with N % 256 == 0 and a 256 x 256 tile for every SM pair: there the int8
+    weights on the 2-SM kernel beat the packed weights on the one-CTA kernel
+    (config-4 out_proj, K 1536: 3.83 -> 3.34 ms per step), while the store-bound
+    K = 768 GEMMs (in_proj, lm_head) are faster packed."""
+    if K < 1536 or N % 256 != 0:
+        return False
+    pairs = _SM_PAIRS.get(dev.index)
+    if pairs is None:
+        pairs = _SM_PAIRS[dev.index] = torch.cuda.get_device_properties(dev).multi_processor_count // 2
+    return (M + 255) // 256 * (N // 256) >= pairs
+
+
 def ternary_matmul(xq: torch.Tensor, tw: TernaryWeights, xs: Optional[torch.Tensor], out=None, out_scale=None,
                    K: Optional[int] = None) -> torch.Tensor:
     """xq int8 [M, K] against the ternary weights, with the BitLinear rescale
-    acc * (w_scale * xs[m]) [* out_scale] (int32 accumulators if xs is None)."""
+    acc * (w_scale * xs[m]) [* out_scale] (int32 accumulators if xs is None).
+    The packed weights, except where the int8 copy on the 2-SM kernel is faster
+    (_pair_kernel_wins); both give the same bits."""
     scale = tw.scale if xs is not None else None
-    if tw.w2 is not None:
+    Kd = xq.shape[1] if K is None else K
+    if tw.w2 is not None and not _pair_kernel_wins(xq.shape[0], tw.w8.shape[0], Kd, xq.device):
         return kernels.bitlinear_packed(xq, tw.w2, xs, scale, out_scale=out_scale, out=out, K=K)
     return kernels.bitlinear_i8(xq, tw.w8, xs, scale, out_scale=out_scale, out=out, K=K)
 
