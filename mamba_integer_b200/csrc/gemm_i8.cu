@@ -45,8 +45,15 @@ constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 template <bool PACKED>
 constexpr int threads_of() { return PACKED ? THREADS_PACKED : THREADS; }
 
-template <int BN, bool PACKED = false>
+// HEAVY (packed 256-wide tiles over K >= 1536, where the tensor cores rather than
+// the output stores set the pace): 12 unpack warps, a 6-slice load ring and one
+// staging box per epilogue warp.  Config 3 (K 2048): 0.2416 against 0.2568 ms;
+// the same setting on the store-bound K = 768 in_proj cost 0.24 ms per step.
+template <int BN, bool PACKED = false, bool HEAVY = false>
 struct Cfg {
+    static constexpr bool H = PACKED && HEAVY && BN > 128;
+    static constexpr int UW = H ? 12 : UNPACK_WARPS;                 // unpack warps (packed only)
+    static constexpr int NTHREADS = THREADS + (PACKED ? 32 * UW : 0);
     static constexpr int A_BYTES = BM * BK;
     static constexpr int B_BYTES = BN * BK;
     static constexpr int P_LOAD = PACKED ? BN * BKP : 0;             // packed bytes the TMA brings per stage
@@ -56,13 +63,13 @@ struct Cfg {
     // int8 tiles, so the load ring (small packed slices) can run deeper and
     // cover the load latency plus the unpack.  256-wide tiles read each A
     // slice once per 256 output columns.
-    static constexpr int STAGES = PACKED ? (BN > 128 ? 5 : 6) : 4;
+    static constexpr int STAGES = PACKED ? (BN > 128 ? (H ? 6 : 5) : 6) : 4;
     static constexpr int STAGE_BYTES = A_BYTES + (PACKED ? P_BYTES : B_BYTES);
     static constexpr int BSTAGES = PACKED ? (BN > 128 ? 2 : 3) : 0;  // int8 weight tiles (packed only)
     static constexpr int BSM = BSTAGES > 0 ? BSTAGES : 1;           // modulus for the ring index
     static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;  // per accumulator
     static constexpr int EPI_BOXES = (BN + 31) / 32;   // 32-column output boxes per tile
-    static constexpr int STG_BUFS = (PACKED || BN > 128) ? 2 : 4;  // staging boxes per epilogue warp
+    static constexpr int STG_BUFS = H ? 1 : ((PACKED || BN > 128) ? 2 : 4);  // staging boxes per epilogue warp
     static constexpr int STG_BYTES = EPI_WARPS * STG_BUFS * 4096;  // (bulk stores kept in flight)
     static constexpr int BAR_BYTES = 256;
     static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BSTAGES * B_BYTES + STG_BYTES + BAR_BYTES;
@@ -191,10 +198,10 @@ __device__ __forceinline__ uint4 unpack16(uint32_t w) {
 // c ^ (r & 7); the tile is 1024-byte aligned).  Each unpack thread takes
 // 16-byte quads of packed bytes (4 words = 4 output chunks of one row), all
 // loads issued before the stores; `tid` counts the unpack threads.
-template <int ROWS>
+template <int ROWS, int UW = UNPACK_WARPS>
 __device__ __forceinline__ void unpack_slice(const unsigned char* packed, unsigned char* tile, int tid) {
     constexpr int QUADS = ROWS * 2;  // a packed row is 2 quads
-    constexpr int NT = 32 * UNPACK_WARPS;
+    constexpr int NT = 32 * UW;
     constexpr int ITERS = (QUADS + NT - 1) / NT;
     uint4 v[ITERS];
 #pragma unroll
@@ -223,13 +230,13 @@ __device__ __forceinline__ void unpack_slice(const unsigned char* packed, unsign
 // share the A row-block in L2).  The smem ring and the two TMEM accumulators
 // carry across tiles, so the epilogue of tile i overlaps the mainloop of
 // tile i+1.
-template <int BN, bool PACKED>
-__global__ void __launch_bounds__(threads_of<PACKED>(), 1)
+template <int BN, bool PACKED, bool HEAVY = false>
+__global__ void __launch_bounds__(Cfg<BN, PACKED, HEAVY>::NTHREADS, 1)
 gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const float* __restrict__ a_scale,
                const float* __restrict__ w_scale, const float* __restrict__ out_scale, int M, int N, int K, int epi,
                unsigned long long* __restrict__ row_stats) {
-    using C = Cfg<BN, PACKED>;
+    using C = Cfg<BN, PACKED, HEAVY>;
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;  // 1024-aligned tiles
@@ -266,7 +273,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             mbar_init(tempty_bar(a), EPI_WARPS);
         }
         for (int b = 0; b < C::BSTAGES; b++) {
-            mbar_init(bready_bar(b), UNPACK_WARPS);
+            mbar_init(bready_bar(b), C::UW);
             mbar_init(bfree_bar(b), 1);
         }
         *abort_flag = 0;
@@ -354,7 +361,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             }
         }
     } else if (PACKED && warp >= 2 + EPI_WARPS) {
-        // ---------------- unpack (warps 6..13) ----------------
+        // ---------------- unpack (warps 6 .. 6 + UW - 1) ----------------
         // Stage g: the packed slice of load slot g % STAGES is expanded into
         // int8 tile g % BSTAGES once that tile's previous MMAs completed.  The
         // load slot itself is released by the MMA commit (which follows this
@@ -372,8 +379,8 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     ok = false;
                     break;
                 }
-                unpack_slice<BN>(gbase + s * C::STAGE_BYTES + C::A_BYTES, gbase + (wring - base) + b * C::B_BYTES,
-                                 tid);
+                unpack_slice<BN, C::UW>(gbase + s * C::STAGE_BYTES + C::A_BYTES,
+                                        gbase + (wring - base) + b * C::B_BYTES, tid);
                 __syncwarp();
                 if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bready_bar(b)) : "memory");
             }
@@ -433,7 +440,7 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
                     }
                 }
                 // the staging buffer used STG_BUFS stores ago must have been read
-                static_assert(C::STG_BUFS == 4 || C::STG_BUFS == 2, "power-of-two staging ring");
+                static_assert(C::STG_BUFS == 4 || C::STG_BUFS == 2 || C::STG_BUFS == 1, "power-of-two staging ring");
                 if (lane == 0) asm volatile("cp.async.bulk.wait_group.read %0;\n" ::"n"(C::STG_BUFS - 1) : "memory");
                 __syncwarp();
                 unsigned char* rowp = stg_g + (nst & (C::STG_BUFS - 1)) * 4096 + lane * 128;
@@ -814,7 +821,7 @@ static int make_wmap(CUtensorMap* tm, const void* W, int N, int K, int box_rows)
     return make_tmap(tm, W, N, K, K, BK, box_rows, 1);
 }
 
-template <int BN, bool PACKED>
+template <int BN, bool PACKED, bool HEAVY = false>
 static int launch(const int8_t* A, int lda, const void* W, const float* a_scale, const float* w_scale,
                   const float* out_scale, void* out, int ldo, int M, int N, int K, int epi, cudaStream_t s,
                   unsigned long long* row_stats = nullptr) {
@@ -827,9 +834,9 @@ static int launch(const int8_t* A, int lda, const void* W, const float* a_scale,
     if (rc) return rc;
     rc = make_tmap(&tc, out, M, N, (long long)ldo * 4, 32, 32, 4);
     if (rc) return rc;
-    using C = Cfg<BN, PACKED>;
-    if (cudaFuncSetAttribute(gemm_i8_kernel<BN, PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
-        cudaSuccess)
+    using C = Cfg<BN, PACKED, HEAVY>;
+    if (cudaFuncSetAttribute(gemm_i8_kernel<BN, PACKED, HEAVY>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::SMEM) != cudaSuccess)
         return MI_ERR_CUDA;
     static int num_sms = 0;
     if (!num_sms) {
@@ -840,7 +847,7 @@ static int launch(const int8_t* A, int lda, const void* W, const float* a_scale,
     }
     const int tiles = cdiv(M, BM) * cdiv(N, BN);
     const int grid = tiles < num_sms ? tiles : num_sms;
-    MI_LAUNCH_DEPENDENT(gemm_i8_kernel<BN, PACKED>, dim3(grid), dim3(threads_of<PACKED>()), C::SMEM, s, ta, tb, tc,
+    MI_LAUNCH_DEPENDENT(gemm_i8_kernel<BN, PACKED, HEAVY>, dim3(grid), dim3(C::NTHREADS), C::SMEM, s, ta, tb, tc,
                         a_scale, w_scale, out_scale, M, N, K, epi, row_stats);
     return MI_OK;
 }
@@ -1230,6 +1237,8 @@ static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_sca
     }
     // the widest N tile that still gives every SM a tile (few-row GEMMs, e.g.
     // decoding, get narrower tiles and more CTAs)
+    if (wide256 && PACKED && K >= 1536)  // tensor-bound packed shapes: the HEAVY setting
+        return launch<256, PACKED, true>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (wide256)
         return launch<256, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (fills(128))
@@ -1381,6 +1390,8 @@ static int bitlinear_norm_sqp(const int8_t* A, int lda, const uint8_t* Wp, const
     if (N <= 32) rc = launch<32, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
     else if (N <= 64) rc = launch<64, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
     else if (N <= 96) rc = launch<96, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
+    else if (N % 256 == 0 && fills(256) && K >= 1536)
+        rc = launch<256, true, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
     else if (N % 256 == 0 && fills(256))
         rc = launch<256, true>(A, lda, Wp, a_scale, w_scale, nullptr, acc, ldc, M, N, K, MI_EPI_I32, s, stats_ws);
     else if (N <= 128 || fills(128))
