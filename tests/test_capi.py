@@ -63,5 +63,16 @@ def test_host_side_argument_errors_need_no_gpu(lib):
     assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, p, 2, (1 << 17) + 1, 4, None) == -2
     assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, None, p, 1, 8, 4, None) == -1
     assert lib.mi_conv_act_quant_noalloc(p, 8, p, p, p, p, None, 1, 8, 4, None) == -1
+    # the decode mid kernels: required pointers, d_state 16, D within the cluster
+    # layout (a multiple of 64 for the packed weights), dt_rank <= 64, 4-byte aligned
+    # packed weights
+    def mid_packed(xz=p, w_x=p, R=48, D=2048, N=16, ldx=4096):
+        return lib.mi_decode_mid_packed(xz, ldx, p, p, p, w_x, p, R, p, p, p, p, None, p, p, 4, D, N, None)
+    assert mid_packed(xz=None) == -1
+    assert mid_packed(N=8) == -2
+    assert mid_packed(D=2080, ldx=4160) == -2
+    assert mid_packed(R=80) == -2
+    assert mid_packed(w_x=p + 2) == -1
+    assert lib.mi_decode_mid(p, 8200, p, p, p, p, p, 48, p, p, p, p, None, p, p, 4, 4100, 16, None) == -2
     assert lib.mi_version() >= 1
     assert lib.mi_status_string(-2) == b"unsupported shape or configuration"
