@@ -1241,6 +1241,15 @@ static int bitlinear(const int8_t* A, int lda, const void* W, const float* a_sca
         return launch<256, PACKED, true>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (wide256)
         return launch<256, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
+    // A GEMM of a few row tiles (decoding) is latency-bound: one wave of 64-wide tiles
+    // on at least half the SMs beats two waves of 32-wide ones (256 decode streams:
+    // in_proj 256 -> 128 tiles, 1.420 -> 1.376 ms per step)
+    auto one_wave = [&](int bn) {
+        const long long t = tm * cdiv(N, bn);
+        return t <= sms && 2 * t >= sms;
+    };
+    if (!fills(128) && one_wave(64))
+        return launch<64, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (fills(128))
         return launch<128, PACKED>(A, lda, W, a_scale, w_scale, out_scale, out, ldo, M, N, K, epilogue, s);
     if (fills(64))
