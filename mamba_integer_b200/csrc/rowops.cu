@@ -253,7 +253,9 @@ static int launch_rowprep(const float* x, const float* delta, const float* res_g
     if (T == 0) return MI_OK;
     rowprep_fn fn = rowprep_table(D / 32);
     if (!fn) return MI_ERR_UNSUPPORTED;
-    const int threads = 256;
+    // one warp per row; few rows (decoding) get 2-warp CTAs so that they spread over
+    // more SMs (256 rows: 128 CTAs instead of 32; 1.379 -> 1.368 ms per decode step)
+    const int threads = T <= 4096 ? 64 : 256;
     int blocks = cdiv(T, threads / 32);
     if (blocks > 148 * 16) blocks = 148 * 16;
     MI_LAUNCH_DEPENDENT(fn, dim3(blocks), dim3(threads), 0, s, x, delta, res_gate, ids, emb, vocab, x_out, gamma, step,
