@@ -161,6 +161,7 @@ quant_rows_kernel(const float* __restrict__ x, int ldx, int T, int K, int8_t* __
                   float* __restrict__ xscale, const float* __restrict__ amax_in, float* __restrict__ clear) {
     const int lane = threadIdx.x & 31;
     const int warps = blockDim.x >> 5;
+    grid_dependency_sync();
     for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < T; t += gridDim.x * warps) {
         const float* row = x + (size_t)t * ldx;
         float amax;
@@ -196,6 +197,7 @@ quant_rows_narrow_kernel(const float* __restrict__ x, int ldx, int T, int K, int
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31, hl = lane & 15, half = lane >> 4;
     const int rows_per_cta = (blockDim.x >> 5) * 2;
+    grid_dependency_sync();
     for (int t0 = blockIdx.x * rows_per_cta; t0 < T; t0 += gridDim.x * rows_per_cta) {
         const int t = t0 + (threadIdx.x >> 5) * 2 + half;
         const bool okr = t < T;
@@ -308,15 +310,13 @@ extern "C" int mi_quantize_rows(const float* x, int ldx, int T, int K, int8_t* x
     if (!amax && K <= 64) {  // narrow rows: two per warp
         int blocks = mi::cdiv(T, threads / 16);
         if (blocks > 148 * 16) blocks = 148 * 16;
-        mi::rowops::quant_rows_narrow_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq,
-                                                                                           xscale, clear);
-        MI_CHECK_LAUNCH();
+        MI_LAUNCH_DEPENDENT(mi::rowops::quant_rows_narrow_kernel, dim3(blocks), dim3(threads), 0, (cudaStream_t)stream,
+                            x, ldx, T, K, xq, ldq, xscale, clear);
         return MI_OK;
     }
     int blocks = mi::cdiv(T, threads / 32);
     if (blocks > 148 * 16) blocks = 148 * 16;
-    mi::rowops::quant_rows_kernel<<<blocks, threads, 0, (cudaStream_t)stream>>>(x, ldx, T, K, xq, ldq, xscale, amax,
-                                                                                clear);
-    MI_CHECK_LAUNCH();
+    MI_LAUNCH_DEPENDENT(mi::rowops::quant_rows_kernel, dim3(blocks), dim3(threads), 0, (cudaStream_t)stream, x, ldx, T,
+                        K, xq, ldq, xscale, amax, clear);
     return MI_OK;
 }

@@ -132,6 +132,7 @@ conv_rows_kernel(const float* __restrict__ xz, int ldx, const float* __restrict_
     const int t0 = blockIdx.x * CONV_TC;
     const bool active = c < D;
     const int cc = active ? c : 0;
+    grid_dependency_sync();
     float4 wv[4];
 #pragma unroll
     for (int e = 0; e < 4; e++) wv[e] = *reinterpret_cast<const float4*>(w + 4 * (cc + e));
@@ -1215,12 +1216,11 @@ extern "C" int mi_conv_act_quant_rows(const float* xz, int ldx, const float* w, 
         return MI_ERR_CUDA;
     }
     if (threads <= 384)
-        mi::ssm::conv_rows_kernel<384><<<grid, threads, ring, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq, xscale,
-                                                                                     L, D);
+        MI_LAUNCH_DEPENDENT(mi::ssm::conv_rows_kernel<384>, grid, dim3(threads), ring, (cudaStream_t)stream, xz, ldx, w,
+                            bias, act, xq, xscale, L, D);
     else
-        mi::ssm::conv_rows_kernel<1024><<<grid, threads, ring, (cudaStream_t)stream>>>(xz, ldx, w, bias, act, xq,
-                                                                                      xscale, L, D);
-    MI_CHECK_LAUNCH();
+        MI_LAUNCH_DEPENDENT(mi::ssm::conv_rows_kernel<1024>, grid, dim3(threads), ring, (cudaStream_t)stream, xz, ldx,
+                            w, bias, act, xq, xscale, L, D);
     return MI_OK;
 }
 
@@ -1246,6 +1246,10 @@ static void launch_scan(int split, int batch, int L, int D, const float* act, co
         cudaFuncSetAttribute(ssm_scan_pipe_kernel<RW>, cudaFuncAttributePreferredSharedMemoryCarveout,
                              cudaSharedmemCarveoutMaxShared);
         dim3 grid(cdiv(D, 32), batch);
+        // Not a dependent launch: launched early, the scan's CTAs are placed wherever the
+        // previous kernel leaves room, and the uneven spread slows this latency-bound
+        // grid when it is a single wave (per-GPU batch 8: 18.6 instead of 14.3 ms per
+        // prefill step).
         ssm_scan_pipe_kernel<RW><<<grid, 128, 0, s>>>(act, bc, ldbc, src, z, ldz, base, y, amax, h_out, L, D);
         return;
     }
