@@ -376,6 +376,25 @@ def test_gemm_pair_kernel_matches_oracle(cuda_dev, M, N, K, monkeypatch):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(16384, 768, 1536), (4096, 768, 1536), (16384, 3072, 768)])
+def test_ternary_matmul_weight_form_rule(cuda_dev, M, N, K):
+    """ternary_matmul takes the int8 copy on the 2-SM kernel for a compute-heavy GEMM
+    (the config-4 out_proj shape, K 1536, at prefill size) and the packed weights
+    otherwise (fewer rows; K 768): either way the bits of the packed kernel."""
+    from mamba_integer_b200.rational_bitnet import TernaryWeights, _pair_kernel_wins, ternary_matmul
+    k = _mi()
+    g = torch.Generator().manual_seed(M + N + K)
+    A = torch.randint(-127, 128, (M, K), generator=g, dtype=torch.int8).to(cuda_dev)
+    W = torch.randint(-1, 2, (N, K), generator=g, dtype=torch.int8).to(cuda_dev)
+    xs = (torch.rand(M, generator=g) * 0.05 + 1e-3).to(cuda_dev)
+    tw = TernaryWeights(W, k.pack_ternary(W), torch.tensor([2.0 ** -6], device=cuda_dev))
+    expect_int8 = (M, N, K) == (16384, 768, 1536)
+    assert _pair_kernel_wins(M, N, K, A.device) == expect_int8
+    got = ternary_matmul(A, tw, xs)
+    ref = k.bitlinear_packed(A, tw.w2, xs, tw.scale)
+    _eq(got, ref, f"ternary_matmul {M}x{N}x{K}")
+
+
 def test_gemm_packed_config3_slice(cuda_dev):
     """Config-3 inputs with the weights packed 2 bits each: a 1024-row slice."""
     from mamba_integer_b200 import synth
