@@ -375,9 +375,12 @@ def server_metrics(dev, n_requests: int = 384, slots: int = 256, max_new: int = 
     lens = [32, 64, 128, 256]
     prompts = [synth.zipf_ids(1, lens[int(torch.randint(0, 4, (1,), generator=g))], cfg["vocab_size"], g)[0].tolist()
                for _ in range(n_requests)]
-    warm = DecodeServer(model, slots=slots)  # capture the step graph and warm the prefill shapes
-    for n in lens:
-        warm.submit(prompts[0][:1] * n, 2)
+    # warm-up: the same request stream served once, untimed (captures the step graph and
+    # meets every admission group's prefill shape, so the allocator holds its buffers);
+    # the timed run then serves it again with a fresh server on the same engine
+    warm = DecodeServer(model, slots=slots)
+    for pr in prompts:
+        warm.submit(pr, max_new)
     warm.run()
     srv = DecodeServer(model, slots=slots, engine=warm.eng)
     torch.cuda.synchronize()

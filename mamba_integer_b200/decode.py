@@ -40,11 +40,14 @@ class StreamStates:
     [n_layer, batch, 3, di] (the inputs at t-3, t-2, t-1) and scan states
     [n_layer, batch, di, 16]."""
 
-    def __init__(self, n_layer: int, batch: int, di: int, N: int, dev):
+    def __init__(self, n_layer: int, batch: int, di: int, N: int, dev, zero: bool = True):
+        # zero=False for states a prompt prefill is about to write in full (the scan writes
+        # every channel's final states, capture_window all three window rows)
         self.batch = batch
         self.di = di
-        self.win = torch.zeros(n_layer, batch, 3, di, dtype=torch.float32, device=dev)
-        self.h = torch.zeros(n_layer, batch, di, N, dtype=torch.float32, device=dev)
+        alloc = torch.zeros if zero else torch.empty
+        self.win = alloc(n_layer, batch, 3, di, dtype=torch.float32, device=dev)
+        self.h = alloc(n_layer, batch, di, N, dtype=torch.float32, device=dev)
 
     def capture_window(self, layer: int, xz: torch.Tensor, batch: int, L: int) -> None:
         """Keep the conv inputs (first di columns of xz) of the last 3 positions."""
@@ -161,7 +164,7 @@ class DecodeEngine:
         they are); returns their last-position logits [k, V]."""
         pre = self.pre
         k = prompt_ids.shape[0]
-        tmp = StreamStates(self.n_layer, k, pre.di, pre.N, pre.dev)
+        tmp = StreamStates(self.n_layer, k, pre.di, pre.N, pre.dev, zero=False)
         logits = pre.forward(prompt_ids.to(pre.dev), states=tmp, last_only=True)
         idx = torch.as_tensor(list(slots), dtype=torch.int64, device=pre.dev)
         self.states.win.index_copy_(1, idx, tmp.win)
