@@ -458,10 +458,14 @@ def test_ssm_scan_matches_oracle(cuda_dev, bsz, L, D, R):
     _eq(amax, np.abs(y_ref).max(axis=1), "row absmax")
 
 
+@pytest.mark.parametrize("bases", ["wide", "below_clamp"])
 @pytest.mark.parametrize("split", [1, 2, 3, 4, 8, 0])
 @pytest.mark.parametrize("bsz,L,D,R", [(2, 70, 512, 16), (1, 300, 1536, 48), (2, 9, 96, 64), (1, 33, 72, 20)])
-def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split):
-    """dt_proj fused into the scan: same result as quantise -> BitLinear -> scan."""
+def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split, bases):
+    """dt_proj fused into the scan: same result as quantise -> BitLinear -> scan.
+    bases "wide": the decay clamp at 32000 binds for some states, and the last
+    channel group takes the step-by-step path; "below_clamp": every base <= 31964
+    (the model initialises them at 16384), where the clamp never binds."""
     k = _mi()
     g = torch.Generator().manual_seed(5 * bsz + L + D + R)
     T = bsz * L
@@ -469,9 +473,14 @@ def test_ssm_scan_fused_dt_matches_oracle(cuda_dev, bsz, L, D, R, split):
     act = torch.rand(T, D, generator=g) * 5
     xp = torch.randn(T, R + 32, generator=g) * 2
     z = torch.randn(T, 2 * D, generator=g) * 3
-    base = torch.randint(29492, 32736, (D, 16), generator=g).float()
-    base[0, :] = 31990.0  # base + mod crosses 32000
-    base[D - 1, :3] = 5.0  # base + mod crosses 0: the step-by-step path for the last channel group
+    if bases == "wide":
+        base = torch.randint(29492, 32736, (D, 16), generator=g).float()
+        base[0, :] = 31990.0  # base + mod crosses 32000
+        base[D - 1, :3] = 5.0  # base + mod crosses 0: the step-by-step path for the last channel group
+    else:
+        base = torch.randint(37, 31965, (D, 16), generator=g).float()
+        base[0, :] = 31964.0  # the largest base without the clamp
+        base[1, :] = 16384.0
     wdt = torch.randint(-1, 2, (D, R), generator=g, dtype=torch.int8)
     ws = np.float32(2.0 ** -5)
     dtq, dts = orc.quant_rows(np.ascontiguousarray(xp[:, :R].numpy()))
