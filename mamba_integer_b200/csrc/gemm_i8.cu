@@ -121,14 +121,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* tm,
         : "memory");
 }
 
-// A hint to bring one tile of a tensor map into L2 (the coordinates follow the
-// loads' rule: x times the element size a multiple of 16 bytes).
-__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* tm, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];\n" ::"l"((uint64_t)tm), "r"(x),
-                 "r"(y)
-                 : "memory");
-}
-
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, uint32_t src, int x, int y) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];\n" ::"l"((uint64_t)tm),
                  "r"(src), "r"(x), "r"(y)
@@ -286,14 +278,6 @@ gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-    }
-    // The first tile's weight slices toward L2 while the previous kernel finishes:
-    // a hint that moves no value into the CTA, so it may precede the dependency wait
-    // whoever writes the weights (they come from HBM in the latency-bound few-row
-    // GEMMs of a decode step, where this overlaps the first round trip).
-    if (threadIdx.x == 32 && (int)blockIdx.x < num_tiles) {
-        const int n0 = ((int)blockIdx.x % tiles_n) * BN;
-        for (int i = 0; i < num_k && i < C::STAGES; i++) tma_prefetch_2d(&tmB, i * (PACKED ? BKP : BK), n0);
     }
     // the previous kernel's outputs (A, the scales) are complete and its TMEM is
     // free before this CTA allocates TMEM or loads anything
