@@ -611,8 +611,12 @@ decode_mid_cluster_kernel(const float* __restrict__ xz, int ldx, const float* __
     for (int i = threadIdx.x; i < DC; i += NT)
         xq[(size_t)b * D + c0 + i] = (int8_t)quant_i8(__fmul_rn(act_s[i], inv_y));
     if (threadIdx.x == 0 && rank == 0) xscale[b] = xs_y;
-    // no CTA leaves while another may still read its shared memory
-    cluster.sync();
+    // No CTA leaves while another may still read its shared memory.  Every remote read
+    // (the partial maxima above) has produced its value before its CTA arrives, and
+    // nothing is handed over here, so the arrive is relaxed: it does not wait for this
+    // CTA's global stores of the row to become visible to the cluster.
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n" ::: "memory");
+    asm volatile("barrier.cluster.wait.aligned;\n" ::: "memory");
 }
 
 // The cluster kernel at the widest CTA (at most one thread per channel of its
